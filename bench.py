@@ -1,0 +1,395 @@
+"""bench.py -- the driver's benchmark contract for the fused-kernel hot path.
+
+Default workload: BASELINE.json configs[1] (C2), the fused elementwise chain
+on fp32 [8192, 8192], forward + autodiff backward, as the fused launch list
+the fusion pass gives.  A step = every launch of that list once, inputs
+resident in HBM (each operand is 256 MiB, twice the 126 MB L2, so no flush is
+needed between steps).  value = algorithmic bytes per step (amendment 33:
+each distinct operand once at its own size, plus the output, summed over
+launches) / device time, summed over ranks.  Multi-GPU: each rank runs its
+own replica (no data-path collective); scaling "weak".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c4|c3]
+  python bench.py --impl reference ...   (the reference's CPU path: the C restatement of interp.js)
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "tensor-compiler-webgpu_b200"
+METRIC = "fused-kernel HBM GB/s (% peak); train tokens/s at 1/2/4/8 B200 vs f64 interp"
+FALLBACK_HBM = 6650.0
+
+
+def _mods():
+    pkg = importlib.import_module(PKG)
+    return (pkg, importlib.import_module(PKG + ".runtime"), importlib.import_module(PKG + ".codegen"),
+            importlib.import_module(PKG + ".workloads"))
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region (reads only)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.path = os.path.join("/tmp", f"tcb_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def build_workload(name, wl, pkg, cg):
+    """(graph, fused, lowered, inputs, keep, config) for a graph workload at its BASELINE size."""
+    if name == "c2":
+        W = wl.c2_graph(8192, 8192)
+        inputs = wl.c2_inputs(W)
+        cfg = {"workload": "C2 elementwise chain fp32 [8192,8192] fwd+bwd", "ops": W["ops"],
+               "row_broadcast": "[1,8192]", "l2": "operands 256 MiB > 126 MB L2, no flush"}
+    elif name == "c4":
+        W = wl.c4_graph(65536, 4096, "softmax")
+        inputs, _ = wl.c4_inputs(W)
+        cfg = {"workload": "C4 softmax fp32 [65536,4096] fwd+bwd, 1% rows +800", "l2": "1 GiB operands > L2"}
+    elif name == "c3":
+        W = wl.c3_graph(4096, 4096, 4096, "relu")
+        inputs = wl.c3_inputs(4096, 4096, 4096)
+        cfg = {"workload": "C3 matmul 4096^3 + bias + relu (fp32)", "l2": "192 MiB operands > L2"}
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    graph = W["graph"]
+    fused = pkg.fuse.fuse(graph, keep=W["keep"])
+    lowered = cg.lower_fused(fused.graph, matmul="tiled" if name == "c3" else "naive")
+    return graph, fused, lowered, inputs, W["keep"], cfg, W
+
+
+def cpu_sample(name, wl, pkg, cg, rows):
+    """The same workload cut to `rows` rows (rows are independent in C2 and C4): graph, inputs, bytes."""
+    if name == "c2":
+        W = wl.c2_graph(rows, 8192)
+        inputs = wl.c2_inputs(W)
+    elif name == "c4":
+        W = wl.c4_graph(rows, 4096, "softmax")
+        inputs, _ = wl.c4_inputs(W)
+    else:
+        W = wl.c3_graph(rows, 4096, 4096, "relu")
+        inputs = wl.c3_inputs(rows, 4096, 4096)
+    fused = pkg.fuse.fuse(W["graph"], keep=W["keep"])
+    nbytes = sum(l.bytes for l in cg.lower_fused(fused.graph)["launches"])
+    return W["graph"], inputs, nbytes
+
+
+def _oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # noqa: the CPU baseline (the reference's algorithm), never the measured GPU path
+    oracle.build()
+    return oracle
+
+
+_SAMPLES = {}
+
+
+def _cpu_worker(job):
+    """One worker's share of a reference-arm step: evaluate its row sample, return (bytes, seconds)."""
+    name, rows, reps = job
+    key = (name, rows)
+    if key not in _SAMPLES:
+        pkg, cg, wl = (importlib.import_module(PKG), importlib.import_module(PKG + ".codegen"),
+                       importlib.import_module(PKG + ".workloads"))
+        _SAMPLES[key] = (_oracle(), *cpu_sample(name, wl, pkg, cg, rows))
+    oracle, graph, inputs, nbytes = _SAMPLES[key]
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.evaluate(graph, inputs, want=[])
+    return nbytes * reps, time.perf_counter() - t0
+
+
+def run_ours(args):
+    world, rank, local = _dist()
+    pkg, rt, cg, wl = _mods()
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    graph, fused, lowered, inputs, keep, cfg, W = build_workload(args.workload, wl, pkg, cg)
+    launches = lowered["launches"]
+    step_bytes = sum(l.bytes for l in launches)
+    runner = rt.GpuRunner.create(local)
+    outs = [fused.index[k] for k in keep]
+    prog = rt.Program(runner, fused.graph, lowered, keep=outs)
+    name_of = {n.id: n.attrs["name"] for n in fused.graph.nodes if n.op == "input"}
+    for nid, name in name_of.items():
+        prog.write(nid, inputs[name])
+    # the dominant kernel: the launch moving the most algorithmic bytes
+    dom = max(range(len(launches)), key=lambda k: launches[k].bytes)
+    seg = rt.Segments(prog, [dom, dom + 1])
+    K, Wm = args.steps, args.warmup
+    ev = rt.Events(runner, 2 * K + 2)
+    kernel_calls = sum(len(l.calls) for l in launches)
+
+    def step(k=None):
+        seg.run(0)
+        if k is not None:
+            ev.record(2 + 2 * k)
+        seg.run(1)
+        if k is not None:
+            ev.record(3 + 2 * k)
+        seg.run(2)
+
+    for _ in range(Wm):
+        step()
+    runner.sync()
+    _barrier(world)
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev.record(0)
+    for k in range(K):
+        step(k)
+    ev.record(1)
+    runner.sync()
+    clk = clocks.stop()
+    total_ms = ev.ms(0, 1)
+    dom_ms = [ev.ms(2 + 2 * k, 3 + 2 * k) for k in range(K)]
+    ms_step = _max_over_ranks(total_ms / K, world)
+    value = world * step_bytes / (ms_step / 1e3) / 1e9
+    peak, peak_kind = _peaks()
+    dom_avg = sum(dom_ms) / K
+    achieved = launches[dom].bytes / (dom_avg / 1e3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            t = json.load(open(tpath)).get(args.workload)
+            if t and t.get("code_hash") == _code_hash(launches[dom].code):
+                traffic = t["dram_bytes_per_launch"]
+        except Exception:
+            traffic = None
+
+    # end to end through the public API: pinned host inputs -> device -> every launch -> outputs to host
+    in_ids = list(name_of)
+    h_in = {nid: rt.PinnedHost(inputs[name_of[nid]].nbytes) for nid in in_ids}
+    for nid in in_ids:
+        h_in[nid].array(inputs[name_of[nid]].size)[:] = inputs[name_of[nid]]
+    out_sizes = {o: pkg.ir.size(fused.graph.nodes[o].shape) for o in outs}
+    h_out = {o: rt.PinnedHost(out_sizes[o] * 4) for o in outs}
+    lib = rt.lib()
+    h2d = sum(h.nbytes for h in h_in.values())
+    d2h = sum(out_sizes[o] * 4 for o in outs)
+    ke = max(1, min(K, args.e2e_steps))
+    ev2 = rt.Events(runner, 2)
+
+    def e2e_step():
+        for nid in in_ids:
+            prog.write_async(nid, h_in[nid].ptr, h_in[nid].nbytes)
+        prog.run()
+        for o in outs:
+            rt.check(lib.tc_memcpy_dtoh(runner.ctx, h_out[o].ptr, prog.ptr(o), out_sizes[o] * 4))
+
+    e2e_step()
+    runner.sync()
+    _barrier(world)
+    ev2.record(0)
+    for _ in range(ke):
+        e2e_step()
+    ev2.record(1)
+    runner.sync()
+    e2e_ms = _max_over_ranks(ev2.ms(0, 1) / ke, world)
+    e2e_value = world * step_bytes / (e2e_ms / 1e3) / 1e9
+
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": Wm,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (mulberry32 seed 0, Box-Muller normals)",
+        "config": {**cfg, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                   "bytes_per_step": step_bytes, "launches_per_step": len(launches)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
+                     "kernel": f"{launches[dom].kind} (launch {dom}, {launches[dom].bytes} algorithmic bytes)",
+                     "kernel_ms": round(dom_avg, 4)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 3), "steps": ke},
+        "gpu_launches": K * kernel_calls,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        result["cpu_baseline"] = cpu_baseline(args.workload, pkg, cg, wl, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    seg.free()
+    ev.free()
+    ev2.free()
+    for h in list(h_in.values()) + list(h_out.values()):
+        h.free()
+    prog.free()
+    runner.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def _code_hash(code):
+    import hashlib
+    return hashlib.sha256(code.encode()).hexdigest()[:16]
+
+
+def cpu_baseline(name, pkg, cg, wl, seconds):
+    """The oracle (C restatement of interp.js, 1 core, -O2) on a bounded row sample; same byte rule."""
+    oracle = _oracle()
+    full = {"c2": 8192, "c4": 65536, "c3": 4096}[name]
+    rows = 8
+    while True:
+        graph, inputs, nbytes = cpu_sample(name, wl, pkg, cg, rows)
+        t0 = time.perf_counter()
+        oracle.evaluate(graph, inputs, want=[])
+        dt = time.perf_counter() - t0
+        if dt * 2 > seconds or rows >= full:
+            break
+        rows = min(full, max(rows * 2, int(rows * seconds / max(dt, 1e-3) / 1.5)))
+    return {"value": round(nbytes / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{rows} of {full} rows, whole graph evaluated once in {dt:.2f} s "
+                      f"(C restatement of interp.js, float64, single thread, gcc -O2)",
+            "seconds": round(dt, 3)}
+
+
+def run_reference(args):
+    """The reference's CPU implementation of the path (the oracle port), all host threads, rank 0 only."""
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    import multiprocessing as mp
+    pkg, _, cg, wl = (importlib.import_module(PKG), None, importlib.import_module(PKG + ".codegen"),
+                      importlib.import_module(PKG + ".workloads"))
+    cores = os.cpu_count() or 1
+    rows = {"c2": 64, "c4": 16, "c3": 1}[args.workload]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        # every worker prepares its sample once (untimed); a step is every worker evaluating it once
+        pool.map(_cpu_worker, [(args.workload, rows, 1)] * cores, chunksize=1)
+        times = []
+        total_bytes = 0
+        for k in range(args.warmup + args.steps):
+            res = pool.map(_cpu_worker, [(args.workload, rows, 1)] * cores, chunksize=1)
+            if k >= args.warmup:
+                times.append(max(t for _, t in res))
+                total_bytes += sum(b for b, _ in res)
+    wall = sum(times)
+    value = total_bytes / wall / 1e9
+    full = {"c2": 8192, "c4": 65536, "c3": 4096}[args.workload]
+    sample = (f"{cores} processes x {rows} of {full} rows per step, step time = slowest process "
+              f"(C restatement of interp.js, float64)")
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * wall / len(times), 2),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+           "data": "synthetic (mulberry32 seed 0)",
+           "config": {"workload": {"c2": "C2 elementwise chain fp32 [8192,8192] fwd+bwd",
+                                   "c4": "C4 softmax fp32 [65536,4096] fwd+bwd, 1% rows +800",
+                                   "c3": "C3 matmul 4096^3 + bias + relu (fp32)"}[args.workload]},
+           "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c3"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

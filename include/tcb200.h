@@ -1,0 +1,148 @@
+/*
+ * tcb200.h -- the C ABI of the B200 backend for the compiler's fused-kernel hot path.
+ *
+ * This is the whole boundary between a host (the reference's JavaScript via a
+ * koffi/N-API binding, or this repository's Python/ctypes host) and the GPU.
+ * It replaces what the reference's src/gpu layer does through WebGPU: device
+ * creation, buffers, shader compilation, dispatch, readback and the
+ * persistent training loop.  Plain C types only: pointers, sizes, handles.
+ *
+ * Conventions
+ *  - Every call returns a tc_status; on failure tc_last_error() gives a
+ *    thread-local message (the reference throws exceptions carrying it:
+ *    src/gpu/runtime.js:61,114-115).
+ *  - A context owns one device's primary CUDA context and one stream.  Calls
+ *    on one context are not thread-safe; use one context per thread.
+ *  - Device addresses are uint64_t; stream handles are uint64_t (a CUstream).
+ *  - Kernels are CUDA C++ source text instantiated from the library's own
+ *    sm_100a templates (the library registers them with NVRTC as headers
+ *    "tcb/elementwise.cuh", "tcb/rowwise.cuh", "tcb/reduce.cuh",
+ *    "tcb/matmul.cuh", "tcb/common.cuh").
+ */
+#ifndef TCB200_H
+#define TCB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tc_status {
+  TC_OK = 0,
+  TC_ERR_INVALID = 1,      /* bad argument or launch geometry, found on the host */
+  TC_ERR_CUDA = 2,         /* a CUDA driver call failed */
+  TC_ERR_COMPILE = 3,      /* NVRTC rejected the source; the log is returned */
+  TC_ERR_OOM = 4,          /* device allocation failed */
+  TC_ERR_TIMEOUT = 5,      /* a bounded wait ran out */
+  TC_ERR_NCCL = 6,         /* a collective failed or was aborted */
+  TC_ERR_UNAVAILABLE = 7   /* a dependency (NCCL) could not be loaded */
+} tc_status;
+
+typedef struct tc_ctx tc_ctx;
+typedef struct tc_buf tc_buf;
+typedef struct tc_module tc_module;
+typedef struct tc_plan tc_plan;
+typedef struct tc_comm tc_comm;
+
+/* Kernel argument block shared by every template: operand pointers, the
+ * output, scratch, and up to 16 integer parameters.  Passed by value. */
+#define TC_MAX_OPERANDS 8
+#define TC_MAX_PARAMS 16
+typedef struct tc_args {
+  uint64_t in[TC_MAX_OPERANDS];
+  uint64_t out;
+  uint64_t scratch;
+  int64_t p[TC_MAX_PARAMS];
+} tc_args;
+
+/* ---- errors, version ---- */
+const char* tc_last_error(void);
+int tc_version(void);
+
+/* ---- device / context: GpuRunner.create() and .info()
+ *      (src/gpu/runtime.js:17-25, :33-41) ---- */
+int tc_open(int device_ordinal, tc_ctx** out);
+int tc_close(tc_ctx* ctx);
+int tc_info(tc_ctx* ctx, char* json, size_t cap);
+int tc_get_stream(tc_ctx* ctx, uint64_t* stream);
+/* Launch on an external stream (e.g. the host framework's current stream); 0 restores the context's own. */
+int tc_set_stream(tc_ctx* ctx, uint64_t stream);
+
+/* ---- buffers: createBuffer / writeBuffer / mapAsync readback and the
+ *      canary padding of GpuRunner.run (src/gpu/runtime.js:12,64-83,116-125) ---- */
+int tc_alloc(tc_ctx* ctx, uint64_t bytes, uint64_t canary_bytes, tc_buf** out);
+int tc_free(tc_buf* buf);
+int tc_buf_ptr(tc_buf* buf, uint64_t* dptr);
+int tc_upload(tc_buf* buf, const void* host, uint64_t bytes, uint64_t offset);
+int tc_download(tc_buf* buf, void* host, uint64_t bytes, uint64_t offset);
+int tc_check_canary(tc_buf* buf, int* intact);
+/* Raw device-address forms (async on the context's stream; host memory should be pinned for overlap). */
+int tc_memcpy_htod(tc_ctx* ctx, uint64_t dst, const void* host, uint64_t bytes);
+int tc_memcpy_dtoh(tc_ctx* ctx, void* host, uint64_t src, uint64_t bytes);
+int tc_memcpy_dtod(tc_ctx* ctx, uint64_t dst, uint64_t src, uint64_t bytes);
+int tc_memset32(tc_ctx* ctx, uint64_t dst, uint32_t value, uint64_t count);
+int tc_host_alloc(uint64_t bytes, void** out);   /* page-locked host memory */
+int tc_host_free(void* p);
+
+/* ---- kernels: GpuRunner.pipeline(code), cached by source text
+ *      (src/gpu/runtime.js:44-52) -- here NVRTC for sm_100a, cached by a hash of the source ---- */
+int tc_compile(tc_ctx* ctx, const char* cuda_src, tc_module** out, char* log, size_t log_cap);
+/* Compile only (no device needed): NVRTC for sm_100a; *cubin_bytes gets the image size. */
+int tc_compile_check(const char* cuda_src, char* log, size_t log_cap, uint64_t* cubin_bytes);
+int tc_module_free(tc_module* mod);
+/* One dispatch (runtime.js:86-101's setPipeline/setBindGroup/dispatchWorkgroups). */
+int tc_launch(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],
+              uint32_t smem_bytes, const tc_args* args);
+/* A dispatch of a TMA-fed kernel: up to 4 fp32 tensor maps (128-byte
+ * swizzle, zero fill out of bounds) are built from 8 values each --
+ * (address, cols, rows, batches, row_stride_bytes, batch_stride_bytes,
+ * box_cols, box_rows) -- and passed, 64-byte aligned, before the tc_args
+ * block.  The address must be 16-byte aligned, the strides multiples of 16
+ * bytes, and box_cols * 4 at most 128. */
+int tc_launch_tma(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],
+                  uint32_t smem_bytes, int n_maps, const uint64_t* map_desc /* 8 per map */,
+                  const tc_args* args);
+
+/* ---- synchronisation and timing ---- */
+int tc_sync(tc_ctx* ctx, int timeout_ms);          /* TC_ERR_TIMEOUT when the wait runs out */
+int tc_event_create(tc_ctx* ctx, uint64_t* ev);
+int tc_event_record(tc_ctx* ctx, uint64_t ev);
+int tc_event_elapsed_ms(uint64_t start, uint64_t end, float* ms);
+int tc_event_destroy(uint64_t ev);
+
+/* ---- plans: the persistent step of GpuTrainer / FusedTrainer
+ *      (src/gpu/trainer.js:33-73, src/fusion/trainer-fused.js:148-185): a launch
+ *      list with resolved addresses, replayed without host work, optionally
+ *      as one CUDA graph ---- */
+int tc_plan_create(tc_ctx* ctx, tc_plan** out);
+int tc_plan_add_launch(tc_plan* plan, tc_module* mod, const char* kernel, const uint32_t grid[3],
+                       const uint32_t block[3], uint32_t smem_bytes, const tc_args* args);
+int tc_plan_add_launch_tma(tc_plan* plan, tc_module* mod, const char* kernel, const uint32_t grid[3],
+                           const uint32_t block[3], uint32_t smem_bytes, int n_maps, const uint64_t* map_desc,
+                           const tc_args* args);
+int tc_plan_add_copy(tc_plan* plan, uint64_t dst, uint64_t src, uint64_t bytes);
+int tc_plan_run(tc_plan* plan);                    /* every entry, in order, on the context's stream */
+int tc_plan_capture(tc_plan* plan);                /* later runs replay one CUDA graph */
+int tc_plan_launch_count(tc_plan* plan, int* n);
+int tc_plan_free(tc_plan* plan);
+
+/* ---- memory planning for a step's arena: interval best-fit over
+ *      (bytes, first_use, last_use) lifetimes; offsets are 256-byte aligned ---- */
+int tc_plan_memory(int n, const uint64_t* bytes, const int32_t* first_use, const int32_t* last_use,
+                   uint64_t* offsets, uint64_t* total);
+
+/* ---- data-parallel collectives (NCCL, loaded at run time) ---- */
+int tc_comm_unique_id(char id[128]);
+int tc_comm_init(tc_ctx* ctx, int rank, int world, const char id[128], int timeout_ms, tc_comm** out);
+/* Sum-allreduce `count` floats in place, then scale by `scale` (fused into the same stream). */
+int tc_allreduce_f32(tc_comm* comm, uint64_t buf, uint64_t count, float scale);
+int tc_comm_wait(tc_comm* comm, int timeout_ms);   /* bounded; aborts the communicator on timeout */
+int tc_comm_abort(tc_comm* comm);
+int tc_comm_destroy(tc_comm* comm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TCB200_H */

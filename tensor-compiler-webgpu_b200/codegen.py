@@ -1,0 +1,789 @@
+"""CUDA source for every launch: the replacement of the reference's WGSL generators.
+
+The reference builds WGSL text per launch (src/gpu/codegen.js:199-215 for
+plain kernels, src/fusion/codegen-fused.js:357-362 for fused nodes).  Here a
+launch is CUDA C++ that instantiates one of libtcb200's hand-written sm_100a
+templates (``tcb/elementwise.cuh``, ``tcb/rowwise.cuh``, ``tcb/matmul.cuh``,
+``tcb/reduce.cuh``) with the fused body emitted as straight-line code:
+
+* every body value is computed once per index it is needed at (the
+  reference's Emitter memoises per index context, codegen-fused.js:80-148);
+* scalar constants are inlined as their exact float32 bits
+  (codegen-fused.js:26-27);
+* shapes and strides are compile-time constants (NVRTC specialises each
+  launch, so index arithmetic is multiply-shift, not the reference's per-axis
+  u32 div/mod loop ``gidx``, codegen-fused.js:47-58);
+* every load is classified -- direct, row broadcast (``i % P``), column
+  broadcast (``i / Q``), scalar, or a general strided gather -- so that direct
+  and row-broadcast loads become 128-bit vector loads.
+"""
+from __future__ import annotations
+
+import math
+import struct
+
+from .ir import size, strides, f32
+
+MAX_RANK = 6  # src/gpu/codegen.js:16, kept for the gather rank limit of the interface
+WG = 256  # threads per CTA of the 1-D templates (the reference's WG = 64, src/gpu/codegen.js:12)
+FUSED_SABOTAGE = ("epilogue-before-bias", "layernorm-tree-short", "softmax-no-max", "fused-bounds-off-by-one")
+
+_BIN = {"add": "tcb::op_add", "sub": "tcb::op_sub", "mul": "tcb::op_mul", "div": "tcb::op_div"}
+_UN = {"neg": "tcb::op_neg", "exp": "tcb::op_exp", "log": "tcb::op_log", "relu": "tcb::op_relu",
+       "tanh": "tcb::op_tanh", "sqrt": "tcb::op_sqrt", "step": "tcb::op_step", "stopGradient": "tcb::op_copy"}
+
+
+def f32_literal(v):
+    """The exact float32 bits of ``fround(v)`` as a CUDA expression (codegen-fused.js:26-27)."""
+    b = struct.unpack("<I", struct.pack("<f", f32(float(v))))[0]
+    return f"tcb::bits(0x{b:08x}u)"
+
+
+def gather_strides(node_op, out_shape, in_shape, perm=None):
+    """Source strides that make a gather over the output read the input (src/gpu/lower.js:31-62)."""
+    if node_op == "broadcast":
+        lead = len(out_shape) - len(in_shape)
+        nat = strides(in_shape)
+        return [0 if (i < lead or in_shape[i - lead] == 1) else nat[i - lead] for i in range(len(out_shape))]
+    if node_op == "transpose":
+        nat = strides(in_shape)
+        return [nat[p] for p in perm]
+    if node_op == "reshape":
+        return strides(out_shape)
+    raise ValueError(f"not a strided move: {node_op}")
+
+
+class Gather:
+    """A strided re-index ``src = sum_d coord_d(i) * g_d`` over an output shape, simplified.
+
+    ``kind``: 'identity' (src = i), 'scalar' (0), 'rowb' (i % P), 'colb' (i / Q),
+    'general'.  Axes of extent 1 are dropped and axes contiguous in both
+    spaces are merged before classifying.
+    """
+
+    def __init__(self, out_shape, gstrides):
+        dims = [(d, g) for d, g in zip(out_shape, gstrides) if d != 1]
+        merged = []
+        for d, g in dims:
+            if merged and merged[-1][1] == g * d and True:
+                pd, pg = merged[-1]
+                merged[-1] = (pd * d, g)
+            elif merged and merged[-1][1] == 0 and g == 0:
+                pd, _ = merged[-1]
+                merged[-1] = (pd * d, 0)
+            else:
+                merged.append((d, g))
+        self.dims = merged
+        nz = [(i, d, g) for i, (d, g) in enumerate(merged) if g != 0]
+        n = len(merged)
+        self.P = self.Q = None
+        if not nz:
+            self.kind = "scalar"
+        elif n == 1 and merged[0][1] == 1:
+            self.kind = "identity"
+        elif len(nz) == 1 and nz[0][0] == n - 1 and nz[0][2] == 1:
+            self.kind = "rowb"
+            self.P = merged[-1][0]
+        elif n == 2 and merged[0][1] == 1 and merged[1][1] == 0:
+            self.kind = "colb"
+            self.Q = merged[1][0]
+        else:
+            self.kind = "general"
+
+    def expr(self, i, T):
+        """C expression of the source index for index expression ``i`` of type T."""
+        if self.kind == "scalar":
+            return f"(({T})0)"
+        if self.kind == "identity":
+            return f"({i})"
+        if self.kind == "rowb":
+            return f"(({i}) % ({T}){self.P}ull)"
+        if self.kind == "colb":
+            return f"(({i}) / ({T}){self.Q}ull)"
+        terms = []
+        ost = 1
+        out = []
+        for d, g in reversed(self.dims):
+            out.append((d, g, ost))
+            ost *= d
+        out.reverse()
+        for k, (d, g, s) in enumerate(out):
+            if g == 0:
+                continue
+            q = f"({i})" if s == 1 else f"(({i}) / ({T}){s}ull)"
+            if k > 0:
+                q = f"({q} % ({T}){d}ull)"
+            terms.append(q if g == 1 else f"{q} * ({T}){g}ull")
+        return "(" + " + ".join(terms) + ")"
+
+    def key(self):
+        return (self.kind, tuple(self.dims))
+
+
+class Ctx:
+    """An index context: the base index, or a gathered index computed from a parent context."""
+
+    def __init__(self, key, parent=None, gather=None):
+        self.key = key
+        self.parent = parent
+        self.gather = gather
+
+
+def idx_type(n):
+    return "u32" if n < 2 ** 32 - 1 else "u64"
+
+
+class Emitter:
+    """Straight-line code for a body graph, memoised per (index context, node).
+
+    ``leaf(k, ctx)`` returns the C expression of operand ``a<k>`` read in
+    ``ctx`` (it registers the load with the template-specific load plan);
+    ``special(nid, ctx)`` may claim a node (the matmul accumulator, a
+    reduction result, a row-tier value).  ``lines`` receives the statements
+    of the current section; the caller may swap it between sections.
+    """
+
+    def __init__(self, body, leaf, special=None):
+        self.b = body
+        self.leaf = leaf
+        self.special = special
+        self.memo = {}
+        self.lines = []
+        self.counter = 0
+        self.ctxs = {}
+
+    def child(self, ctx, gather):
+        if gather.kind == "identity":
+            return ctx
+        key = (ctx.key, gather.key())
+        c = self.ctxs.get(key)
+        if c is None:
+            c = self.ctxs[key] = Ctx(key, ctx, gather)
+        return c
+
+    def forget(self, pred):
+        for k in [k for k in self.memo if pred(k[0])]:
+            del self.memo[k]
+
+    def value(self, nid, ctx):
+        key = (ctx.key, nid)
+        if key in self.memo:
+            return self.memo[key]
+        if self.special is not None:
+            s = self.special(nid, ctx)
+            if s is not None:
+                self.memo[key] = s
+                return s
+        node = self.b.nodes[nid]
+        op = node.op
+        if op == "input":
+            v = self.leaf(int(node.attrs["name"][1:]), ctx)
+            self.memo[key] = v
+            return v
+        if op == "const":
+            val = node.attrs["value"]
+            v = f32_literal(val if isinstance(val, (int, float)) else val[0])
+            self.memo[key] = v
+            return v
+        if op == "reshape":
+            v = self.value(node.inputs[0], ctx)
+            self.memo[key] = v
+            return v
+        if op in ("broadcast", "transpose"):
+            src = self.b.nodes[node.inputs[0]]
+            if src.op == "const":
+                v = self.value(src.id, ctx)
+            else:
+                g = Gather(node.shape, gather_strides(op, node.shape, src.shape, node.attrs.get("perm")))
+                v = self.value(src.id, self.child(ctx, g))
+            self.memo[key] = v
+            return v
+        if op in _BIN:
+            a = self.value(node.inputs[0], ctx)
+            c = self.value(node.inputs[1], ctx)
+            expr = f"{_BIN[op]}({a}, {c})"
+        elif op in _UN:
+            expr = f"{_UN[op]}({self.value(node.inputs[0], ctx)})"
+        else:
+            raise ValueError(f"fused codegen: no rule for '{op}'")
+        name = f"v{self.counter}"
+        self.counter += 1
+        self.lines.append(f"const float {name} = {expr};")
+        self.memo[key] = name
+        return name
+
+
+def _chain_index(ctx, base, T):
+    """The C index expression of ``ctx`` given the base context's index expression."""
+    if ctx.parent is None:
+        return base
+    return ctx.gather.expr(_chain_index(ctx.parent, base, T), T)
+
+
+def _operand_count(body):
+    return sum(1 for n in body.nodes if n.op == "input")
+
+
+# ------------------------------------------------------------------ elementwise
+class _EwLoads:
+    """Load plan of the elementwise template: W lanes starting at i0."""
+
+    def __init__(self, W, T):
+        self.W, self.T = W, T
+        self.fields = []   # declarations in Regs<W>
+        self.stmts = []    # load statements
+        self.per_lane = []  # per-lane load statements
+        self.seen = {}
+
+    def leaf(self, k, ctx):
+        key = (ctx.key, k)
+        if key in self.seen:
+            return self.seen[key]
+        W, T = self.W, self.T
+        ptr = f"reinterpret_cast<const float*>(a.in[{k}])"
+        name = f"x{len(self.seen)}"
+        g = ctx.gather
+        if ctx.parent is None:
+            self.fields.append(f"float {name}[W];")
+            self.stmts.append(f"tcb::load<W>(r.{name}, {ptr} + i0);")
+            ref = f"r.{name}[l]"
+        elif ctx.parent.parent is None and g.kind == "rowb" and g.P % 4 == 0:
+            self.fields.append(f"float {name}[W];")
+            self.stmts.append(f"tcb::load<W>(r.{name}, {ptr} + (({T})i0 % ({T}){g.P}ull));")
+            ref = f"r.{name}[l]"
+        elif ctx.parent.parent is None and (g.kind == "scalar" or (g.kind == "colb" and g.Q % 4 == 0)):
+            self.fields.append(f"float {name};")
+            self.stmts.append(f"r.{name} = tcb::ld1({ptr} + {g.expr(f'({T})i0', T)});")
+            ref = f"r.{name}"
+        else:
+            self.fields.append(f"float {name}[W];")
+            self.per_lane.append(f"r.{name}[l] = tcb::ld1({ptr} + {_chain_index(ctx, f'(({T})i0 + ({T})l)', T)});")
+            ref = f"r.{name}[l]"
+        self.seen[key] = ref
+        return ref
+
+
+def _elementwise_source(body, out_id, n, sabotage=None, tag="elementwise"):
+    T = idx_type(n)
+    loads = _EwLoads("W", T)
+    em = Emitter(body, loads.leaf)
+    base = Ctx("i")
+    out = em.value(out_id, base)
+    fields = "\n    ".join(loads.fields) or "float unused_;"
+    stmts = "\n    ".join(loads.stmts)
+    lanes = "\n      ".join(loads.per_lane)
+    per_lane = f"#pragma unroll\n    for (int l = 0; l < W; ++l) {{\n      {lanes}\n    }}" if loads.per_lane else ""
+    comp = "\n      ".join(em.lines)
+    src = f"""// {tag}: generated from a body of {len(body.nodes)} nodes, {n} elements
+#include "tcb/common.cuh"
+#define TCB_W 4
+struct Body {{
+  template <int W> struct Regs {{
+    {fields}
+  }};
+  template <int W> __device__ __forceinline__ static void load(const tcb::Args& a, u64 i0, Regs<W>& r) {{
+    {stmts}
+    {per_lane}
+  }}
+  template <int W> __device__ __forceinline__ static void compute(const Regs<W>& r, float (&o)[W]) {{
+#pragma unroll
+    for (int l = 0; l < W; ++l) {{
+      {comp}
+      o[l] = {out};
+    }}
+  }}
+}};
+#include "tcb/elementwise.cuh"
+"""
+    return src
+
+
+# ------------------------------------------------------------------ rowwise
+def _pow2ceil(x):
+    return 1 << max(0, math.ceil(math.log2(max(1, x))))
+
+
+def rowwise_geometry(R, C, n_leaves, elems_per_thread=16):
+    """Threads per row, rows per CTA, vector width, register slots; cache or stream mode."""
+    vec = 4 if C % 4 == 0 else 1
+    tpr = min(1024, max(32, _pow2ceil(math.ceil(C / elems_per_thread))))
+    groups = max(1, 256 // tpr)
+    slots = math.ceil(C / (tpr * vec))
+    items = slots * vec
+    cache = items <= 32 and items * max(1, n_leaves) <= 128
+    return {"vec": vec, "tpr": tpr, "groups": groups, "slots": slots, "items": items, "cache": cache,
+            "block": tpr * groups}
+
+
+class _RowLoads:
+    """Load plan of the rowwise template: row leaves (once per row) and element leaves (per item)."""
+
+    def __init__(self, body, R, C, T, vec, cache):
+        self.body, self.R, self.C, self.T, self.vec, self.cache = body, R, C, T, vec, cache
+        self.row = {}      # key -> (name, stmt)
+        self.elem = {}     # key -> (name, kind, stmt-builder)
+        self.order_row = []
+        self.order_elem = []
+
+    def leaf(self, k, ctx):
+        T = self.T
+        ptr = f"reinterpret_cast<const float*>(a.in[{k}])"
+        if ctx.key == "r":
+            key = ("r", k)
+            if key not in self.row:
+                name = f"R{len(self.row)}"
+                self.row[key] = name
+                self.order_row.append(f"const float {name} = active ? tcb::ld1({ptr} + ({T})r) : 0.0f;")
+            return self.row[key]
+        # element context (or a gathered child of it)
+        g = ctx.gather
+        if ctx.parent is not None and ctx.parent.key == "e" and g.kind == "colb" and g.Q == self.C:
+            return self.leaf(k, Ctx("r"))
+        key = (ctx.key, k)
+        if key in self.elem:
+            return self.elem[key]
+        name = f"L{len(self.elem)}"
+        vec = self.vec
+        if ctx.key == "e":
+            kind, idx = "vec", "e"
+        elif ctx.parent is not None and ctx.parent.key == "e" and g.kind == "rowb" and g.P % 4 == 0:
+            kind, idx = "vec", f"(e % ({T}){g.P}ull)"
+        elif ctx.parent is not None and ctx.parent.key == "e" and (g.kind == "scalar" or (g.kind == "colb" and g.Q % 4 == 0)):
+            kind, idx = "one", g.expr("e", T)
+        else:
+            kind, idx = "lane", _chain_index(ctx, f"(e + ({T})l)", T)
+        if vec == 1 and kind == "vec":
+            kind = "lane"
+            idx = idx if idx != "e" else "(e + l)"
+        self.order_elem.append((name, kind, ptr, idx))
+        ref = f"{name}[q]" if self.cache else f"{name}[l]"
+        self.elem[key] = ref
+        return ref
+
+    def load_stmts(self, slot_var):
+        """Statements loading every element leaf of one slot (c, e defined; q base = slot*VEC)."""
+        out = []
+        V = self.vec
+        for name, kind, ptr, idx in self.order_elem:
+            dst = f"{name}[{slot_var} * {V} + l]" if self.cache else f"{name}[l]"
+            if kind == "vec":
+                out.append(f"{{ float t_[{V}]; tcb::load<{V}>(t_, {ptr} + {idx});"
+                           f" _Pragma(\"unroll\") for (int l = 0; l < {V}; ++l) {dst} = t_[l]; }}")
+            elif kind == "one":
+                out.append(f"{{ const float t_ = tcb::ld1({ptr} + {idx});"
+                           f" _Pragma(\"unroll\") for (int l = 0; l < {V}; ++l) {dst} = t_; }}")
+            else:
+                out.append(f"_Pragma(\"unroll\") for (int l = 0; l < {V}; ++l) {dst} = tcb::ld1({ptr} + {idx});")
+        return out
+
+
+def _rowwise_walk(body, loads, reductions, out_id, row_tier, pattern, sabotage, TPR, GROUPS):
+    """Emit every phase of a rowwise body: [(row_lines, elem_lines, k, init, combine, reduce_expr)], output."""
+    reduced = {}
+    em = _row_emitter(body, loads, reduced, row_tier)
+    E, ROW = Ctx("e"), Ctx("r")
+    phases = []
+    for k, rd in enumerate(reductions):
+        em.forget(lambda key: key != "r")
+        em.lines, em.row_lines = [], []
+        v = em.value(rd.inputs[0], E)
+        is_max = rd.op == "max"
+        red = f"tcb::group_reduce<{TPR}, {GROUPS}, {'true' if is_max else 'false'}>(acc{k}, red)"
+        if sabotage == "layernorm-tree-short" and pattern == "layernorm":
+            red = f"acc{k}"  # the bug: the cross-thread tree is skipped
+        if sabotage == "softmax-no-max" and is_max and pattern in ("softmax", "log-softmax"):
+            red = f"((void){red}, 0.0f)"  # the bug: the shift is never taken
+        phases.append((list(em.row_lines), list(em.lines), k,
+                       "-__int_as_float(0x7f800000)" if is_max else "0.0f",
+                       f"tcb::op_max(acc{k}, {v})" if is_max else f"tcb::op_add(acc{k}, {v})", red))
+        reduced[rd.id] = f"red{k}"
+        em.memo[("r", rd.id)] = f"red{k}"
+    em.forget(lambda key: key != "r")
+    em.lines, em.row_lines = [], []
+    out_row = row_tier(out_id)
+    ov = em.value(out_id, ROW if out_row else E)
+    return phases, (list(em.row_lines), list(em.lines), ov, out_row)
+
+
+def _rowwise_source(body, out_id, pattern, sabotage=None):
+    """A fused rowwise kernel (template tcb/rowwise.cuh; reference codegen-fused.js:271-354)."""
+    reductions = [n for n in body.nodes if n.op in ("sum", "max")]
+    S = body.nodes[reductions[0].inputs[0]].shape
+    C = S[-1]
+    R = size(S) // C
+    T = idx_type(R * C)
+
+    def row_tier(nid):
+        s = size(body.nodes[nid].shape)
+        return s == R and s != R * C
+
+    # a dry run counts the element-tier leaves, which sets the register budget
+    geo = rowwise_geometry(R, C, 1)
+    dry = _RowLoads(body, R, C, T, geo["vec"], True)
+    _rowwise_walk(body, dry, reductions, out_id, row_tier, pattern, None, geo["tpr"], geo["groups"])
+    geo = rowwise_geometry(R, C, len(dry.order_elem))
+    V, TPR, GROUPS, SLOTS, ITEMS, CACHE = (geo[k] for k in ("vec", "tpr", "groups", "slots", "items", "cache"))
+    loads = _RowLoads(body, R, C, T, V, CACHE)
+    phases, (orow, oelem, ov, out_row) = _rowwise_walk(body, loads, reductions, out_id, row_tier, pattern,
+                                                        sabotage, TPR, GROUPS)
+
+    def lines(xs, ind):
+        return ("\n" + " " * ind).join(xs)
+
+    def item_loop(elem_lines, tail, store):
+        """Per-element code over this thread's elements of the row; `store` writes o_[] per slot."""
+        if CACHE:
+            head = f"""_Pragma("unroll")
+      for (int s = 0; s < {SLOTS}; ++s) {{
+        const u32 c = (u32)(s * {TPR} + t) * {V};
+        if (active && c < {C}u) {{
+          const {T} e = ({T})r * ({T}){C} + c; (void)e;"""
+            foot = "        }\n      }"
+            qdef = f"const int q = s * {V} + l; (void)q;"
+        else:
+            decl = " ".join(f"float {nm}[{V}];" for nm, _, _, _ in loads.order_elem)
+            head = f"""for (u32 c = (u32)t * {V}; active && c < {C}u; c += {TPR * V}u) {{
+        {{
+          const {T} e = ({T})r * ({T}){C} + c; (void)e;
+          {decl}
+          {lines(loads.load_stmts("0"), 10)}"""
+            foot = "        }\n      }"
+            qdef = ""
+        body_ = f"""
+          {"float o_[" + str(V) + "];" if store else ""}
+          _Pragma("unroll")
+          for (int l = 0; l < {V}; ++l) {{
+            {qdef}
+            {lines(elem_lines + tail, 12)}
+          }}
+          {f"tcb::store<{V}>(out + e, o_);" if store else ""}
+"""
+        return head + body_ + foot
+
+    parts = []
+    for row_lines, elem_lines, k, init, comb, red in phases:
+        parts.append(lines(row_lines, 6))
+        parts.append(f"float acc{k} = {init};")
+        parts.append(item_loop(elem_lines, [f"acc{k} = {comb};"], False))
+        parts.append(f"const float red{k} = {red};")
+    parts.append(lines(orow, 6))
+    if out_row:
+        parts.append(f"if (active && t == 0) out[r] = {ov};")
+    else:
+        parts.append(item_loop(oelem, [f"o_[l] = {ov};"], True))
+    cache_decl = cache_load = ""
+    if CACHE and loads.order_elem:
+        cache_decl = " ".join(f"float {nm}[{ITEMS}];" for nm, _, _, _ in loads.order_elem)
+        zero = " ".join(f"{nm}[s * {V} + l] = 0.0f;" for nm, _, _, _ in loads.order_elem)
+        cache_load = f"""_Pragma("unroll")
+    for (int s = 0; s < {SLOTS}; ++s) {{
+      const u32 c = (u32)(s * {TPR} + t) * {V};
+      const {T} e = ({T})r * ({T}){C} + c; (void)e;
+      if (active && c < {C}u) {{
+        {lines(loads.load_stmts("s"), 8)}
+      }} else {{
+        _Pragma("unroll") for (int l = 0; l < {V}; ++l) {{ {zero} }}
+      }}
+    }}"""
+    nw = max(1, TPR // 32)
+    src = f"""// rowwise ({pattern}): R={R} C={C}, {TPR} threads per row, {GROUPS} rows per CTA, vec {V}, {'cached' if CACHE else 'streamed'}
+#include "tcb/common.cuh"
+#include "tcb/rowwise.cuh"
+extern "C" __global__ void __launch_bounds__({TPR * GROUPS}) tcb_rowwise(const tcb::Args a) {{
+  __shared__ float red[{GROUPS * nw}];
+  float* __restrict__ out = reinterpret_cast<float*>(a.out);
+  const int g = threadIdx.x / {TPR};
+  const int t = threadIdx.x % {TPR};
+  for (u64 row0 = (u64)blockIdx.x * {GROUPS}; row0 < {R}ull; row0 += (u64)gridDim.x * {GROUPS}) {{
+    const u64 r = row0 + g;
+    const bool active = r < {R}ull;
+    {lines(loads.order_row, 4)}
+    {cache_decl}
+    {cache_load}
+      {lines([p for p in parts if p], 6)}
+  }}
+}}
+"""
+    return src, geo, R, C
+
+
+def _row_emitter(body, loads, reduced, row_tier):
+    em = Emitter(body, loads.leaf)
+    em.row_lines = []
+
+    def special(nid, ctx):
+        node = body.nodes[nid]
+        if nid in reduced:
+            return reduced[nid]
+        if ctx.key == "e" and row_tier(nid):
+            return _row_value(em, nid)
+        if ctx.key == "e" and node.op == "broadcast":
+            src = body.nodes[node.inputs[0]]
+            if row_tier(src.id) and src.op not in ("input", "const"):
+                return _row_value(em, src.id)
+        return None
+
+    em.special = special
+    return em
+
+
+def _row_value(em, nid):
+    """A row-tier value: computed in the row context, its statements hoisted before the item loop."""
+    key = ("r", nid)
+    if key in em.memo:
+        return em.memo[key]
+    saved = em.lines
+    em.lines = []
+    v = em.value(nid, Ctx("r"))
+    em.row_lines.extend(em.lines)
+    em.lines = saved
+    return v
+
+
+# ------------------------------------------------------------------ matmul epilogue
+def _epilogue_source(body, out_id, sabotage=None, kernel="simt"):
+    root = next(n for n in body.nodes if n.op == "matmul")
+    ia, ib = (int(body.nodes[i].attrs["name"][1:]) for i in root.inputs)
+    a_s, b_s = body.nodes[root.inputs[0]].shape, body.nodes[root.inputs[1]].shape
+    batch, M, K, N = size(a_s[:-2]), a_s[-2], a_s[-1], b_s[-1]
+    bias_add = None
+    if sabotage == "epilogue-before-bias":
+        for n in body.nodes:
+            if n.op == "add" and root.id in n.inputs and not all(i == root.id for i in n.inputs):
+                if n.id != out_id:
+                    bias_add = n
+                break
+    lines = []
+    seen = {}
+
+    def leaf(k, ctx):
+        key = (ctx.key, k)
+        if key not in seen:
+            name = f"x{len(seen)}"
+            seen[key] = name
+            lines.append(f"const float {name} = tcb::ld1(reinterpret_cast<const float*>(a.in[{k}]) + "
+                         f"{_chain_index(ctx, 'i', 'u64')});")
+        return seen[key]
+
+    def special(nid, ctx):
+        if ctx.key == "i" and (nid == root.id or (bias_add is not None and nid == bias_add.id)):
+            return "acc"
+        return None
+
+    em = Emitter(body, leaf, special)
+    em.lines = lines
+    base = Ctx("i")
+    out = em.value(out_id, base)
+    if bias_add is not None:
+        other = next(i for i in bias_add.inputs if i != root.id)
+        out = f"tcb::op_add({out}, {em.value(other, base)})"
+    code = "\n    ".join(lines)
+    src = f"""// matmul epilogue ({kernel}): batch {batch}, [{M},{K}] x [{K},{N}]
+#include "tcb/common.cuh"
+#define TCB_M {M}
+#define TCB_N {N}
+#define TCB_K {K}
+#define TCB_BATCH {batch}
+#define TCB_IA {ia}
+#define TCB_IB {ib}
+struct Epi {{
+  __device__ __forceinline__ static float apply(const tcb::Args& a, float acc, u64 i, u64 row, u64 col, u64 b) {{
+    (void)row; (void)col; (void)b;
+    {code}
+    return {out};
+  }}
+}};
+#include "tcb/matmul.cuh"
+"""
+    return src, (batch, M, K, N)
+
+
+# ------------------------------------------------------------------ plain reduce
+SM_COUNT = 148
+
+
+def _reduce_source(op, in_shape, axis):
+    outer = size(in_shape[:axis])
+    n = in_shape[axis]
+    inner = size(in_shape[axis + 1:])
+    outs = outer * inner
+    split = 1
+    if inner > 1 and outs < 2 * SM_COUNT * 256 and n >= 64:
+        split = max(1, min(math.ceil(n / 32), math.ceil(SM_COUNT * 2048 / max(1, outs))))
+    src = f"""// {op} over axis {axis} of {list(in_shape)}: outer {outer}, n {n}, inner {inner}, split {split}
+#include "tcb/common.cuh"
+#define TCB_OUTER {outer}
+#define TCB_N {n}
+#define TCB_INNER {inner}
+#define TCB_SPLIT {split}
+#define TCB_IS_MAX {1 if op == 'max' else 0}
+#include "tcb/reduce.cuh"
+"""
+    return src, (outer, n, inner, split)
+
+
+# ------------------------------------------------------------------ launches
+class KernelCall:
+    """One kernel launch of a Launch: entry name, grid, block, dynamic smem, p[] parameters."""
+    __slots__ = ("name", "grid", "block", "smem", "params")
+
+    def __init__(self, name, grid, block, smem=0, params=()):
+        self.name, self.grid, self.block, self.smem, self.params = name, tuple(grid), tuple(block), smem, list(params)
+
+    def __repr__(self):
+        return f"KernelCall({self.name}, grid={self.grid}, block={self.block})"
+
+
+class Launch:
+    """One node's work: the reference's launch record ``{node, op, kind, pattern, inputs, params, grid, code}``
+    (src/gpu/lower.js:108-111, src/fusion/lower-fused.js:37-41) with CUDA source and kernel calls."""
+    __slots__ = ("node", "op", "kind", "pattern", "inputs", "code", "calls", "scratch_bytes", "bytes", "info")
+
+    def __init__(self, node, op, kind, pattern, inputs, code, calls, scratch_bytes=0, info=None):
+        self.node, self.op, self.kind, self.pattern = node, op, kind, pattern
+        self.inputs = list(inputs)
+        self.code = code
+        self.calls = calls
+        self.scratch_bytes = scratch_bytes
+        self.bytes = 0
+        self.info = info or {}
+
+    def __repr__(self):
+        return f"Launch(node={self.node}, kind={self.kind}, pattern={self.pattern}, calls={len(self.calls)})"
+
+
+def grid1d(n, per_thread=4, block=WG, waves=8):
+    """CTAs for a grid-stride 1-D kernel over n elements (at most `waves` CTAs per SM)."""
+    chunks = max(1, math.ceil(n / per_thread))
+    return (max(1, min(math.ceil(chunks / block), SM_COUNT * waves)), 1, 1)
+
+
+def _ew_launch(body, out_id, n, kind, node_id, op, pattern, inputs, sabotage=None, tag="elementwise"):
+    code = _elementwise_source(body, out_id, n, tag=tag)
+    count = n + 1 if sabotage == "fused-bounds-off-by-one" else n
+    call = KernelCall("tcb_elementwise", grid1d(n), (WG, 1, 1), 0, [count])
+    return Launch(node_id, op, kind, pattern, inputs, code, [call])
+
+
+def _epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, matmul, sabotage=None):
+    code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage)
+    if batch > 65535:
+        raise ValueError("matmul batch above 65535")
+    call = KernelCall("tcb_matmul", (math.ceil(N / 128), math.ceil(M / 128), batch), (256, 1, 1), 0, [])
+    return Launch(node_id, op, kind, pattern, inputs, code, [call], info={"mnk": (batch, M, K, N)})
+
+
+def _rowwise_launch(body, out_id, node_id, pattern, inputs, sabotage=None):
+    code, geo, R, C = _rowwise_source(body, out_id, pattern, sabotage)
+    rows_per_cta = geo["groups"]
+    ctas = max(1, min(math.ceil(R / rows_per_cta), SM_COUNT * max(1, 2048 // geo["block"]) * 4))
+    call = KernelCall("tcb_rowwise", (ctas, 1, 1), (geo["block"], 1, 1), 0, [])
+    return Launch(node_id, "fused", "fused-rowwise", pattern, inputs, code, [call], info={"R": R, "C": C, **geo})
+
+
+def _reduce_launch(op, in_shape, axis, node_id, inputs):
+    code, (outer, n, inner, split) = _reduce_source(op, in_shape, axis)
+    outs = outer * inner
+    if inner == 1:
+        calls = [KernelCall("tcb_reduce_rows", (max(1, min(math.ceil(outer * 32 / 256), SM_COUNT * 8)), 1, 1),
+                            (256, 1, 1))]
+        scratch = 0
+    else:
+        gx = max(1, min(math.ceil(outs / 256), SM_COUNT * 8))
+        calls = [KernelCall("tcb_reduce_cols", (gx, split, 1), (256, 1, 1))]
+        scratch = 0
+        if split > 1:
+            calls.append(KernelCall("tcb_reduce_finish", (max(1, min(math.ceil(outs / 256), SM_COUNT * 8)), 1, 1),
+                                    (256, 1, 1)))
+            scratch = split * outs * 4
+    return Launch(node_id, op, op, None, inputs, code, calls, scratch_bytes=scratch,
+                  info={"outer": outer, "n": n, "inner": inner, "split": split})
+
+
+def _one_op_body(op, in_shapes, attrs):
+    from .ir import Graph
+    g = Graph()
+    ins = [g.input(f"a{k}", s) for k, s in enumerate(in_shapes)]
+    out = g.emit(op, ins, attrs)
+    return g, out
+
+
+def _plain_launch_uncached(op, in_shapes, attrs, matmul):
+    body, out = _one_op_body(op, in_shapes, attrs)
+    n = size(body.nodes[out].shape)
+    if op in ("sum", "max"):
+        return _reduce_launch(op, in_shapes[0], attrs["axis"], -1, [])
+    if op == "matmul":
+        return _epilogue_launch(body, out, -1, "matmul", f"matmul-{matmul}", None, [], matmul)
+    if op in _BIN or op in _UN:
+        kind = "copy" if op == "stopGradient" else op
+        return _ew_launch(body, out, n, kind, -1, op, None, [], tag=f"plain {op}")
+    if op in ("broadcast", "transpose", "reshape"):
+        return _ew_launch(body, out, n, "gather", -1, op, None, [], tag=f"plain {op} (gather)")
+    raise ValueError(f"no lowering for '{op}'")
+
+
+_plain_cache = {}
+
+
+def _plain_launch(graph, node, matmul):
+    """The launch one node gets alone, cached by (op, shapes, attrs, matmul) (src/fusion/lower-fused.js:13-25)."""
+    import json
+    shapes = [list(graph.nodes[i].shape) for i in node.inputs]
+    key = json.dumps([node.op, shapes, node.attrs, matmul], sort_keys=True)
+    one = _plain_cache.get(key)
+    if one is None:
+        one = _plain_cache[key] = _plain_launch_uncached(node.op, shapes, node.attrs, matmul)
+    lau = Launch(node.id, node.op, one.kind, None, node.inputs, one.code, one.calls, one.scratch_bytes, one.info)
+    return lau
+
+
+def _bytes(graph, lau):
+    """Amendment 33 (src/fusion/workloads.js:170-172): each distinct operand once at its own size, plus the output."""
+    b = sum(size(graph.nodes[i].shape) * 4 for i in dict.fromkeys(lau.inputs))
+    return b + size(graph.nodes[lau.node].shape) * 4
+
+
+def lower(graph, matmul="naive", sabotage=None):
+    """One launch per op, no fusion (src/gpu/lower.js:68-114)."""
+    launches = []
+    for node in graph.nodes:
+        if node.op in ("input", "const"):
+            continue
+        lau = _plain_launch(graph, node, matmul)
+        lau.bytes = _bytes(graph, lau)
+        launches.append(lau)
+    return {"launches": launches}
+
+
+def fused_kernel(node, matmul="naive", sabotage=None):
+    """The launch of a fused node (src/fusion/codegen-fused.js:357-362)."""
+    from .fuse import body_of
+    body = body_of(node)
+    out = node.attrs["output"]
+    kind = node.attrs["kind"]
+    sab = sabotage if sabotage in FUSED_SABOTAGE else None
+    if kind == "elementwise":
+        return _ew_launch(body, out, size(node.shape), "fused-elementwise", node.id, "fused", node.attrs["pattern"],
+                          node.inputs, sab, tag=f"fused elementwise ({len(node.inputs)} operands)")
+    if kind == "epilogue":
+        return _epilogue_launch(body, out, node.id, "fused", "fused-epilogue", node.attrs["pattern"], node.inputs,
+                                matmul, sab)
+    if kind == "rowwise":
+        return _rowwise_launch(body, out, node.id, node.attrs["pattern"], node.inputs, sab)
+    raise ValueError(f"no fused kernel kind '{kind}'")
+
+
+def lower_fused(graph, matmul="naive", sabotage=None):
+    """A fused node to its kernel, every other node to its plain launch (src/fusion/lower-fused.js:32-45)."""
+    launches = []
+    for node in graph.nodes:
+        if node.op in ("input", "const"):
+            continue
+        if node.op == "fused":
+            lau = fused_kernel(node, matmul, sabotage)
+        else:
+            lau = _plain_launch(graph, node, matmul)
+        lau.bytes = _bytes(graph, lau)
+        launches.append(lau)
+    return {"launches": launches}

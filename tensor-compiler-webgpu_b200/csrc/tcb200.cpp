@@ -1,0 +1,702 @@
+// libtcb200: the C-ABI runtime of the B200 backend (declared in include/tcb200.h).
+//
+// CUDA driver API on the device's primary context (so pointers and streams
+// interoperate with any runtime-API user of the same device), NVRTC for the
+// per-fused-node kernels, NCCL loaded with dlopen for the data-parallel
+// allreduce.  No call blocks without a bound; every failure is a status plus
+// a thread-local message.
+#include <cuda.h>
+#include <dlfcn.h>
+#include <nvrtc.h>
+
+#include "cuapi.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/tcb200.h"
+#include "tcb_templates.inc"  // generated: kTemplates[] = {name, text}
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[2048];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return status;
+}
+
+const char* cu_name(CUresult r) {
+  const char* s = nullptr;
+  CU(cuGetErrorName)(r, &s);
+  return s ? s : "CUDA_ERROR_UNKNOWN";
+}
+
+#define CU_TRY(call)                                                                 \
+  do {                                                                               \
+    CUresult _r = (call);                                                            \
+    if (_r != CUDA_SUCCESS) {                                                        \
+      if (_r == CUDA_ERROR_OUT_OF_MEMORY) return fail(TC_ERR_OOM, "%s: %s", #call, cu_name(_r)); \
+      return fail(TC_ERR_CUDA, "%s: %s", #call, cu_name(_r));                       \
+    }                                                                                \
+  } while (0)
+
+uint64_t fnv1a(const char* s, size_t n) {
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < n; i++) { h ^= (unsigned char)s[i]; h *= 1099511628211ull; }
+  return h;
+}
+
+}  // namespace
+
+struct tc_module {
+  tc_ctx* ctx = nullptr;
+  CUmodule mod = nullptr;
+  std::map<std::string, CUfunction> fns;
+  int refs = 1;
+};
+
+struct tc_ctx {
+  int ordinal = 0;
+  CUdevice dev = 0;
+  CUcontext cu = nullptr;
+  CUstream own_stream = nullptr;
+  CUstream stream = nullptr;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  std::map<uint64_t, tc_module*> cache;  // source hash -> module
+  std::map<uint64_t, std::string> cache_src;
+};
+
+struct tc_buf {
+  tc_ctx* ctx = nullptr;
+  CUdeviceptr ptr = 0;
+  uint64_t bytes = 0;
+  uint64_t canary = 0;
+};
+
+static const uint32_t kCanary = 0xdeadbeefu;
+
+static int bind(tc_ctx* ctx) {
+  if (!ctx) return fail(TC_ERR_INVALID, "null context");
+  CU_TRY(CU(cuCtxSetCurrent)(ctx->cu));
+  return TC_OK;
+}
+
+extern "C" {
+
+const char* tc_last_error(void) { return g_err.c_str(); }
+int tc_version(void) { return 1; }
+
+int tc_open(int device_ordinal, tc_ctx** out) {
+  if (!out) return fail(TC_ERR_INVALID, "null out");
+  *out = nullptr;
+  if (!tcb_cu().ok) return fail(TC_ERR_UNAVAILABLE, "no CUDA driver: libcuda.so.1 could not be loaded");
+  CU_TRY(CU(cuInit)(0));
+  int n = 0;
+  CU_TRY(CU(cuDeviceGetCount)(&n));
+  if (device_ordinal < 0 || device_ordinal >= n)
+    return fail(TC_ERR_INVALID, "device %d not present (%d devices)", device_ordinal, n);
+  auto ctx = std::make_unique<tc_ctx>();
+  ctx->ordinal = device_ordinal;
+  CU_TRY(CU(cuDeviceGet)(&ctx->dev, device_ordinal));
+  CU_TRY(CU(cuDevicePrimaryCtxRetain)(&ctx->cu, ctx->dev));
+  CU_TRY(CU(cuCtxSetCurrent)(ctx->cu));
+  CU_TRY(CU(cuDeviceGetAttribute)(&ctx->sm_count, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, ctx->dev));
+  CU_TRY(CU(cuDeviceGetAttribute)(&ctx->cc_major, CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MAJOR, ctx->dev));
+  CU_TRY(CU(cuDeviceGetAttribute)(&ctx->cc_minor, CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MINOR, ctx->dev));
+  if (ctx->cc_major != 10 || ctx->cc_minor != 0) {
+    CU(cuDevicePrimaryCtxRelease)(ctx->dev);
+    return fail(TC_ERR_UNAVAILABLE, "device %d is sm_%d%d; this library is built for sm_100a only", device_ordinal,
+                ctx->cc_major, ctx->cc_minor);
+  }
+  CU_TRY(CU(cuStreamCreate)(&ctx->own_stream, CU_STREAM_NON_BLOCKING));
+  ctx->stream = ctx->own_stream;
+  *out = ctx.release();
+  return TC_OK;
+}
+
+int tc_close(tc_ctx* ctx) {
+  if (!ctx) return TC_OK;
+  CU(cuCtxSetCurrent)(ctx->cu);
+  CU(cuStreamSynchronize)(ctx->stream);
+  for (auto& kv : ctx->cache) {
+    if (kv.second->mod) CU(cuModuleUnload)(kv.second->mod);
+    delete kv.second;
+  }
+  if (ctx->own_stream) CU(cuStreamDestroy)(ctx->own_stream);
+  CU(cuDevicePrimaryCtxRelease)(ctx->dev);
+  delete ctx;
+  return TC_OK;
+}
+
+int tc_info(tc_ctx* ctx, char* json, size_t cap) {
+  if (int s = bind(ctx)) return s;
+  char name[256] = {0};
+  CU_TRY(CU(cuDeviceGetName)(name, sizeof name, ctx->dev));
+  size_t mem = 0;
+  CU_TRY(CU(cuDeviceTotalMem)(&mem, ctx->dev));
+  int drv = 0;
+  CU_TRY(CU(cuDriverGetVersion)(&drv));
+  int smem_optin = 0, clock = 0, l2 = 0;
+  CU(cuDeviceGetAttribute)(&smem_optin, CU_DEVICE_ATTRIBUTE_MAX_SHARED_MEMORY_PER_BLOCK_OPTIN, ctx->dev);
+  CU(cuDeviceGetAttribute)(&l2, CU_DEVICE_ATTRIBUTE_L2_CACHE_SIZE, ctx->dev);
+  int nvrtc_major = 0, nvrtc_minor = 0;
+  nvrtcVersion(&nvrtc_major, &nvrtc_minor);
+  int n = snprintf(json, cap,
+                   "{\"device\": \"%s\", \"ordinal\": %d, \"sm\": \"sm_%d%d\", \"sm_count\": %d, "
+                   "\"memory_bytes\": %zu, \"l2_bytes\": %d, \"smem_optin_bytes\": %d, \"driver\": %d, "
+                   "\"nvrtc\": \"%d.%d\", \"kernels_cached\": %zu}",
+                   name, ctx->ordinal, ctx->cc_major, ctx->cc_minor, ctx->sm_count, mem, l2, smem_optin, drv,
+                   nvrtc_major, nvrtc_minor, ctx->cache.size());
+  (void)clock;
+  if (n < 0 || (size_t)n >= cap) return fail(TC_ERR_INVALID, "info buffer too small");
+  return TC_OK;
+}
+
+int tc_get_stream(tc_ctx* ctx, uint64_t* stream) {
+  if (!ctx || !stream) return fail(TC_ERR_INVALID, "null argument");
+  *stream = (uint64_t)(uintptr_t)ctx->stream;
+  return TC_OK;
+}
+
+int tc_set_stream(tc_ctx* ctx, uint64_t stream) {
+  if (!ctx) return fail(TC_ERR_INVALID, "null context");
+  ctx->stream = stream ? (CUstream)(uintptr_t)stream : ctx->own_stream;
+  return TC_OK;
+}
+
+// ---------------------------------------------------------------- buffers
+int tc_alloc(tc_ctx* ctx, uint64_t bytes, uint64_t canary_bytes, tc_buf** out) {
+  if (!out) return fail(TC_ERR_INVALID, "null out");
+  *out = nullptr;
+  if (int s = bind(ctx)) return s;
+  canary_bytes = (canary_bytes + 3) / 4 * 4;
+  uint64_t total = std::max<uint64_t>(4, (bytes + 3) / 4 * 4 + canary_bytes);
+  auto b = std::make_unique<tc_buf>();
+  b->ctx = ctx;
+  b->bytes = bytes;
+  b->canary = canary_bytes;
+  CU_TRY(CU(cuMemAlloc)(&b->ptr, total));
+  if (canary_bytes) {
+    uint64_t off = (bytes + 3) / 4 * 4;
+    CUresult r = CU(cuMemsetD32Async)(b->ptr + off, kCanary, canary_bytes / 4, ctx->stream);
+    if (r != CUDA_SUCCESS) { CU(cuMemFree)(b->ptr); return fail(TC_ERR_CUDA, "canary fill: %s", cu_name(r)); }
+    // the bytes between `bytes` and the 4-byte boundary keep the pattern too
+    if (bytes % 4) {
+      uint32_t w = kCanary;
+      r = CU(cuMemcpyHtoDAsync)(b->ptr + bytes / 4 * 4, &w, 4, ctx->stream);
+      if (r == CUDA_SUCCESS) r = CU(cuStreamSynchronize)(ctx->stream);
+      if (r != CUDA_SUCCESS) { CU(cuMemFree)(b->ptr); return fail(TC_ERR_CUDA, "canary fill: %s", cu_name(r)); }
+    }
+  }
+  *out = b.release();
+  return TC_OK;
+}
+
+int tc_free(tc_buf* buf) {
+  if (!buf) return TC_OK;
+  CU(cuCtxSetCurrent)(buf->ctx->cu);
+  CUresult r = CU(cuMemFree)(buf->ptr);
+  delete buf;
+  if (r != CUDA_SUCCESS) return fail(TC_ERR_CUDA, "cuMemFree: %s", cu_name(r));
+  return TC_OK;
+}
+
+int tc_buf_ptr(tc_buf* buf, uint64_t* dptr) {
+  if (!buf || !dptr) return fail(TC_ERR_INVALID, "null argument");
+  *dptr = (uint64_t)buf->ptr;
+  return TC_OK;
+}
+
+int tc_upload(tc_buf* buf, const void* host, uint64_t bytes, uint64_t offset) {
+  if (!buf || (!host && bytes)) return fail(TC_ERR_INVALID, "null argument");
+  if (offset + bytes > buf->bytes) return fail(TC_ERR_INVALID, "upload of %llu bytes at %llu past a %llu-byte buffer",
+                                               (unsigned long long)bytes, (unsigned long long)offset,
+                                               (unsigned long long)buf->bytes);
+  if (int s = bind(buf->ctx)) return s;
+  CU_TRY(CU(cuMemcpyHtoDAsync)(buf->ptr + offset, host, bytes, buf->ctx->stream));
+  CU_TRY(CU(cuStreamSynchronize)(buf->ctx->stream));
+  return TC_OK;
+}
+
+int tc_download(tc_buf* buf, void* host, uint64_t bytes, uint64_t offset) {
+  if (!buf || (!host && bytes)) return fail(TC_ERR_INVALID, "null argument");
+  if (offset + bytes > buf->bytes + buf->canary)
+    return fail(TC_ERR_INVALID, "download past the end of the buffer");
+  if (int s = bind(buf->ctx)) return s;
+  CU_TRY(CU(cuMemcpyDtoHAsync)(host, buf->ptr + offset, bytes, buf->ctx->stream));
+  CU_TRY(CU(cuStreamSynchronize)(buf->ctx->stream));
+  return TC_OK;
+}
+
+int tc_check_canary(tc_buf* buf, int* intact) {
+  if (!buf || !intact) return fail(TC_ERR_INVALID, "null argument");
+  *intact = 1;
+  if (!buf->canary && buf->bytes % 4 == 0) return TC_OK;
+  if (int s = bind(buf->ctx)) return s;
+  uint64_t start = buf->bytes / 4 * 4;
+  uint64_t words = ((buf->bytes + 3) / 4 * 4 + buf->canary - start) / 4;
+  std::vector<uint32_t> h(words);
+  CU_TRY(CU(cuMemcpyDtoHAsync)(h.data(), buf->ptr + start, words * 4, buf->ctx->stream));
+  CU_TRY(CU(cuStreamSynchronize)(buf->ctx->stream));
+  for (uint64_t i = (buf->bytes % 4) ? 1 : 0; i < words; i++)
+    if (h[i] != kCanary) { *intact = 0; break; }
+  if (buf->bytes % 4) {  // the partial word: only its tail bytes are padding
+    const unsigned char* p = (const unsigned char*)h.data();
+    const unsigned char* c = (const unsigned char*)&kCanary;
+    for (uint64_t k = buf->bytes % 4; k < 4; k++) if (p[k] != c[k]) *intact = 0;
+  }
+  return TC_OK;
+}
+
+int tc_memcpy_htod(tc_ctx* ctx, uint64_t dst, const void* host, uint64_t bytes) {
+  if (int s = bind(ctx)) return s;
+  if (bytes) CU_TRY(CU(cuMemcpyHtoDAsync)((CUdeviceptr)dst, host, bytes, ctx->stream));
+  return TC_OK;
+}
+
+int tc_memcpy_dtoh(tc_ctx* ctx, void* host, uint64_t src, uint64_t bytes) {
+  if (int s = bind(ctx)) return s;
+  if (bytes) CU_TRY(CU(cuMemcpyDtoHAsync)(host, (CUdeviceptr)src, bytes, ctx->stream));
+  return TC_OK;
+}
+
+int tc_memcpy_dtod(tc_ctx* ctx, uint64_t dst, uint64_t src, uint64_t bytes) {
+  if (int s = bind(ctx)) return s;
+  if (bytes) CU_TRY(CU(cuMemcpyDtoDAsync)((CUdeviceptr)dst, (CUdeviceptr)src, bytes, ctx->stream));
+  return TC_OK;
+}
+
+int tc_memset32(tc_ctx* ctx, uint64_t dst, uint32_t value, uint64_t count) {
+  if (int s = bind(ctx)) return s;
+  if (count) CU_TRY(CU(cuMemsetD32Async)((CUdeviceptr)dst, value, count, ctx->stream));
+  return TC_OK;
+}
+
+int tc_host_alloc(uint64_t bytes, void** out) {
+  if (!out) return fail(TC_ERR_INVALID, "null out");
+  CU_TRY(CU(cuInit)(0));
+  CUcontext cur = nullptr;
+  CU(cuCtxGetCurrent)(&cur);
+  if (!cur) return fail(TC_ERR_INVALID, "tc_host_alloc needs an open context on this thread");
+  CU_TRY(CU(cuMemHostAlloc)(out, std::max<uint64_t>(bytes, 1), CU_MEMHOSTALLOC_PORTABLE));
+  return TC_OK;
+}
+
+int tc_host_free(void* p) {
+  if (p) CU_TRY(CU(cuMemFreeHost)(p));
+  return TC_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- kernels
+namespace {
+
+struct TmaBlock {
+  alignas(64) CUtensorMap maps[4];
+  tc_args args;
+};
+
+int get_fn(tc_module* mod, const char* name, CUfunction* fn) {
+  auto it = mod->fns.find(name);
+  if (it != mod->fns.end()) { *fn = it->second; return TC_OK; }
+  CUresult r = CU(cuModuleGetFunction)(fn, mod->mod, name);
+  if (r != CUDA_SUCCESS) return fail(TC_ERR_INVALID, "kernel '%s' not in module: %s", name, cu_name(r));
+  mod->fns[name] = *fn;
+  return TC_OK;
+}
+
+int check_geometry(tc_ctx* ctx, const uint32_t grid[3], const uint32_t block[3], uint32_t smem) {
+  (void)ctx;
+  if (!grid || !block) return fail(TC_ERR_INVALID, "null grid or block");
+  uint64_t threads = (uint64_t)block[0] * block[1] * block[2];
+  if (threads == 0 || threads > 1024) return fail(TC_ERR_INVALID, "block of %llu threads", (unsigned long long)threads);
+  if (grid[0] == 0 || grid[1] == 0 || grid[2] == 0) return fail(TC_ERR_INVALID, "empty grid");
+  if (grid[1] > 65535 || grid[2] > 65535) return fail(TC_ERR_INVALID, "grid y/z above 65535");
+  if (smem > 232448) return fail(TC_ERR_INVALID, "%u bytes of shared memory requested", smem);
+  return TC_OK;
+}
+
+int prepare_smem(CUfunction fn, uint32_t smem) {
+  if (smem > 48 * 1024) {
+    CU_TRY(CU(cuFuncSetAttribute)(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem));
+  }
+  return TC_OK;
+}
+
+int encode_maps(int n_maps, const uint64_t* d, TmaBlock* blk) {
+  if (n_maps < 0 || n_maps > 4) return fail(TC_ERR_INVALID, "%d tensor maps (at most 4)", n_maps);
+  for (int m = 0; m < n_maps; m++) {
+    const uint64_t* v = d + 8 * m;
+    uint64_t addr = v[0], cols = v[1], rows = v[2], batches = v[3], rs = v[4], bs = v[5], bc = v[6], br = v[7];
+    if (addr % 16) return fail(TC_ERR_INVALID, "tensor map %d: address not 16-byte aligned", m);
+    if (rs % 16 || bs % 16) return fail(TC_ERR_INVALID, "tensor map %d: strides must be multiples of 16 bytes", m);
+    if (bc * 4 > 128 || bc == 0 || br == 0 || br > 256) return fail(TC_ERR_INVALID, "tensor map %d: bad box", m);
+    if (cols == 0 || rows == 0 || batches == 0) return fail(TC_ERR_INVALID, "tensor map %d: empty", m);
+    cuuint64_t dims[3] = {cols, rows, batches};
+    cuuint64_t strides[2] = {rs, bs};
+    cuuint32_t box[3] = {(cuuint32_t)bc, (cuuint32_t)br, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = CU(cuTensorMapEncodeTiled)(&blk->maps[m], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)addr, dims, strides,
+                                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TC_ERR_INVALID, "cuTensorMapEncodeTiled (map %d): %s", m, cu_name(r));
+  }
+  return TC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+static int nvrtc_build(const char* src, char* log, size_t log_cap, std::vector<char>* cubin) {
+  if (log && log_cap) log[0] = 0;
+  std::vector<const char*> hdr_text, hdr_name;
+  for (size_t i = 0; i < sizeof(kTemplates) / sizeof(kTemplates[0]); i++) {
+    hdr_name.push_back(kTemplates[i].name);
+    hdr_text.push_back(kTemplates[i].text);
+  }
+  nvrtcProgram prog;
+  nvrtcResult nr = nvrtcCreateProgram(&prog, src, "tcb_kernel.cu", (int)hdr_text.size(), hdr_text.data(), hdr_name.data());
+  if (nr != NVRTC_SUCCESS) return fail(TC_ERR_COMPILE, "nvrtcCreateProgram: %s", nvrtcGetErrorString(nr));
+  const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17", "-lineinfo", "--device-as-default-execution-space",
+                        "-DTCB_NVRTC=1"};
+  nr = nvrtcCompileProgram(prog, (int)(sizeof opts / sizeof opts[0]), opts);
+  size_t log_size = 0;
+  nvrtcGetProgramLogSize(prog, &log_size);
+  std::string plog(log_size, '\0');
+  if (log_size) nvrtcGetProgramLog(prog, &plog[0]);
+  if (log && log_cap) {
+    size_t n = std::min(log_cap - 1, plog.size());
+    memcpy(log, plog.data(), n);
+    log[n] = 0;
+  }
+  if (nr != NVRTC_SUCCESS) {
+    nvrtcDestroyProgram(&prog);
+    return fail(TC_ERR_COMPILE, "NVRTC: %s\n%s", nvrtcGetErrorString(nr), plog.c_str());
+  }
+  size_t cubin_size = 0;
+  nvrtcGetCUBINSize(prog, &cubin_size);
+  cubin->resize(cubin_size);
+  nvrtcGetCUBIN(prog, cubin->data());
+  nvrtcDestroyProgram(&prog);
+  return TC_OK;
+}
+
+int tc_compile_check(const char* src, char* log, size_t log_cap, uint64_t* cubin_bytes) {
+  if (!src) return fail(TC_ERR_INVALID, "null source");
+  std::vector<char> cubin;
+  if (int s = nvrtc_build(src, log, log_cap, &cubin)) return s;
+  if (cubin_bytes) *cubin_bytes = cubin.size();
+  return TC_OK;
+}
+
+int tc_compile(tc_ctx* ctx, const char* src, tc_module** out, char* log, size_t log_cap) {
+  if (!out || !src) return fail(TC_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (int s = bind(ctx)) return s;
+  size_t len = strlen(src);
+  uint64_t h = fnv1a(src, len);
+  auto it = ctx->cache.find(h);
+  if (it != ctx->cache.end() && ctx->cache_src[h] == src) {
+    it->second->refs++;
+    *out = it->second;
+    return TC_OK;
+  }
+  std::vector<char> cubin;
+  if (int s = nvrtc_build(src, log, log_cap, &cubin)) return s;
+  auto mod = std::make_unique<tc_module>();
+  mod->ctx = ctx;
+  CUresult r = CU(cuModuleLoadData)(&mod->mod, cubin.data());
+  if (r != CUDA_SUCCESS) return fail(TC_ERR_CUDA, "cuModuleLoadData: %s", cu_name(r));
+  mod->refs = 2;  // the cache's reference and the caller's
+  ctx->cache[h] = mod.get();
+  ctx->cache_src[h] = src;
+  *out = mod.release();
+  return TC_OK;
+}
+
+int tc_module_free(tc_module* mod) {
+  if (!mod) return TC_OK;
+  mod->refs--;  // the context's cache keeps the module until tc_close
+  return TC_OK;
+}
+
+int tc_launch(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3], uint32_t smem,
+              const tc_args* args) {
+  if (!mod || !kernel || !args) return fail(TC_ERR_INVALID, "null argument");
+  if (int s = bind(mod->ctx)) return s;
+  if (int s = check_geometry(mod->ctx, grid, block, smem)) return s;
+  CUfunction fn;
+  if (int s = get_fn(mod, kernel, &fn)) return s;
+  if (int s = prepare_smem(fn, smem)) return s;
+  tc_args a = *args;
+  void* params[] = {&a};
+  CU_TRY(CU(cuLaunchKernel)(fn, grid[0], grid[1], grid[2], block[0], block[1], block[2], smem, mod->ctx->stream, params,
+                        nullptr));
+  return TC_OK;
+}
+
+int tc_launch_tma(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3], uint32_t smem,
+                  int n_maps, const uint64_t* map_desc, const tc_args* args) {
+  if (!mod || !kernel || !args || (n_maps && !map_desc)) return fail(TC_ERR_INVALID, "null argument");
+  if (int s = bind(mod->ctx)) return s;
+  if (int s = check_geometry(mod->ctx, grid, block, smem)) return s;
+  CUfunction fn;
+  if (int s = get_fn(mod, kernel, &fn)) return s;
+  if (int s = prepare_smem(fn, smem)) return s;
+  TmaBlock blk;
+  memset(&blk, 0, sizeof blk);
+  if (int s = encode_maps(n_maps, map_desc, &blk)) return s;
+  blk.args = *args;
+  void* params[] = {&blk};
+  CU_TRY(CU(cuLaunchKernel)(fn, grid[0], grid[1], grid[2], block[0], block[1], block[2], smem, mod->ctx->stream, params,
+                        nullptr));
+  return TC_OK;
+}
+
+// ---------------------------------------------------------------- sync, events
+int tc_sync(tc_ctx* ctx, int timeout_ms) {
+  if (int s = bind(ctx)) return s;
+  CUevent ev;
+  CU_TRY(CU(cuEventCreate)(&ev, CU_EVENT_DISABLE_TIMING));
+  CUresult r = CU(cuEventRecord)(ev, ctx->stream);
+  if (r != CUDA_SUCCESS) { CU(cuEventDestroy)(ev); return fail(TC_ERR_CUDA, "cuEventRecord: %s", cu_name(r)); }
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    r = CU(cuEventQuery)(ev);
+    if (r == CUDA_SUCCESS) break;
+    if (r != CUDA_ERROR_NOT_READY) { CU(cuEventDestroy)(ev); return fail(TC_ERR_CUDA, "stream: %s", cu_name(r)); }
+    double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (timeout_ms >= 0 && ms > timeout_ms) {
+      CU(cuEventDestroy)(ev);
+      return fail(TC_ERR_TIMEOUT, "stream not done after %d ms", timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(ms < 5 ? 10 : 200));
+  }
+  CU(cuEventDestroy)(ev);
+  return TC_OK;
+}
+
+int tc_event_create(tc_ctx* ctx, uint64_t* ev) {
+  if (!ev) return fail(TC_ERR_INVALID, "null out");
+  if (int s = bind(ctx)) return s;
+  CUevent e;
+  CU_TRY(CU(cuEventCreate)(&e, CU_EVENT_DEFAULT));
+  *ev = (uint64_t)(uintptr_t)e;
+  return TC_OK;
+}
+
+int tc_event_record(tc_ctx* ctx, uint64_t ev) {
+  if (int s = bind(ctx)) return s;
+  CU_TRY(CU(cuEventRecord)((CUevent)(uintptr_t)ev, ctx->stream));
+  return TC_OK;
+}
+
+int tc_event_elapsed_ms(uint64_t start, uint64_t end, float* ms) {
+  if (!ms) return fail(TC_ERR_INVALID, "null out");
+  CU_TRY(CU(cuEventSynchronize)((CUevent)(uintptr_t)end));
+  CU_TRY(CU(cuEventElapsedTime)(ms, (CUevent)(uintptr_t)start, (CUevent)(uintptr_t)end));
+  return TC_OK;
+}
+
+int tc_event_destroy(uint64_t ev) {
+  if (ev) CU_TRY(CU(cuEventDestroy)((CUevent)(uintptr_t)ev));
+  return TC_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- plans
+struct tc_plan {
+  tc_ctx* ctx = nullptr;
+  struct Entry {
+    int kind = 0;  // 0 launch, 1 launch with tensor maps, 2 copy
+    CUfunction fn = nullptr;
+    uint32_t grid[3] = {1, 1, 1}, block[3] = {1, 1, 1}, smem = 0;
+    tc_args args = {};
+    std::shared_ptr<TmaBlock> tma;
+    uint64_t dst = 0, src = 0, bytes = 0;
+  };
+  std::vector<Entry> entries;
+  CUgraph graph = nullptr;
+  CUgraphExec exec = nullptr;
+  CUstream captured_on = nullptr;
+};
+
+extern "C" {
+
+int tc_plan_create(tc_ctx* ctx, tc_plan** out) {
+  if (!ctx || !out) return fail(TC_ERR_INVALID, "null argument");
+  *out = new tc_plan();
+  (*out)->ctx = ctx;
+  return TC_OK;
+}
+
+static int plan_add(tc_plan* plan, tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],
+                    uint32_t smem, int n_maps, const uint64_t* map_desc, const tc_args* args, bool tma) {
+  if (!plan || !mod || !kernel || !args) return fail(TC_ERR_INVALID, "null argument");
+  if (plan->exec) return fail(TC_ERR_INVALID, "plan already captured");
+  if (int s = bind(plan->ctx)) return s;
+  if (int s = check_geometry(plan->ctx, grid, block, smem)) return s;
+  tc_plan::Entry e;
+  if (int s = get_fn(mod, kernel, &e.fn)) return s;
+  if (int s = prepare_smem(e.fn, smem)) return s;
+  e.kind = tma ? 1 : 0;
+  for (int i = 0; i < 3; i++) { e.grid[i] = grid[i]; e.block[i] = block[i]; }
+  e.smem = smem;
+  e.args = *args;
+  if (tma) {
+    e.tma = std::make_shared<TmaBlock>();
+    memset(e.tma.get(), 0, sizeof(TmaBlock));
+    if (int s = encode_maps(n_maps, map_desc, e.tma.get())) return s;
+    e.tma->args = *args;
+  }
+  plan->entries.push_back(e);
+  return TC_OK;
+}
+
+int tc_plan_add_launch(tc_plan* plan, tc_module* mod, const char* kernel, const uint32_t grid[3],
+                       const uint32_t block[3], uint32_t smem, const tc_args* args) {
+  return plan_add(plan, mod, kernel, grid, block, smem, 0, nullptr, args, false);
+}
+
+int tc_plan_add_launch_tma(tc_plan* plan, tc_module* mod, const char* kernel, const uint32_t grid[3],
+                           const uint32_t block[3], uint32_t smem, int n_maps, const uint64_t* map_desc,
+                           const tc_args* args) {
+  return plan_add(plan, mod, kernel, grid, block, smem, n_maps, map_desc, args, true);
+}
+
+int tc_plan_add_copy(tc_plan* plan, uint64_t dst, uint64_t src, uint64_t bytes) {
+  if (!plan) return fail(TC_ERR_INVALID, "null plan");
+  if (plan->exec) return fail(TC_ERR_INVALID, "plan already captured");
+  tc_plan::Entry e;
+  e.kind = 2;
+  e.dst = dst; e.src = src; e.bytes = bytes;
+  plan->entries.push_back(e);
+  return TC_OK;
+}
+
+static int plan_issue(tc_plan* plan) {
+  CUstream st = plan->ctx->stream;
+  for (auto& e : plan->entries) {
+    if (e.kind == 2) {
+      if (e.bytes) CU_TRY(CU(cuMemcpyDtoDAsync)((CUdeviceptr)e.dst, (CUdeviceptr)e.src, e.bytes, st));
+      continue;
+    }
+    void* params[1];
+    tc_args a = e.args;
+    if (e.kind == 1) params[0] = e.tma.get();
+    else params[0] = &a;
+    CU_TRY(CU(cuLaunchKernel)(e.fn, e.grid[0], e.grid[1], e.grid[2], e.block[0], e.block[1], e.block[2], e.smem, st,
+                          params, nullptr));
+  }
+  return TC_OK;
+}
+
+int tc_plan_run(tc_plan* plan) {
+  if (!plan) return fail(TC_ERR_INVALID, "null plan");
+  if (int s = bind(plan->ctx)) return s;
+  if (plan->exec) {
+    if (plan->captured_on != plan->ctx->stream) {
+      // graphs replay on any stream of the context
+    }
+    CU_TRY(CU(cuGraphLaunch)(plan->exec, plan->ctx->stream));
+    return TC_OK;
+  }
+  return plan_issue(plan);
+}
+
+int tc_plan_capture(tc_plan* plan) {
+  if (!plan) return fail(TC_ERR_INVALID, "null plan");
+  if (int s = bind(plan->ctx)) return s;
+  if (plan->exec) return TC_OK;
+  CUstream st = plan->ctx->stream;
+  CU_TRY(CU(cuStreamBeginCapture)(st, CU_STREAM_CAPTURE_MODE_THREAD_LOCAL));
+  int s = plan_issue(plan);
+  CUgraph g = nullptr;
+  CUresult r = CU(cuStreamEndCapture)(st, &g);
+  if (s) { if (g) CU(cuGraphDestroy)(g); return s; }
+  if (r != CUDA_SUCCESS) return fail(TC_ERR_CUDA, "cuStreamEndCapture: %s", cu_name(r));
+  r = CU(cuGraphInstantiate)(&plan->exec, g, 0);
+  if (r != CUDA_SUCCESS) { CU(cuGraphDestroy)(g); return fail(TC_ERR_CUDA, "cuGraphInstantiate: %s", cu_name(r)); }
+  plan->graph = g;
+  plan->captured_on = st;
+  return TC_OK;
+}
+
+int tc_plan_launch_count(tc_plan* plan, int* n) {
+  if (!plan || !n) return fail(TC_ERR_INVALID, "null argument");
+  int k = 0;
+  for (auto& e : plan->entries) if (e.kind != 2) k++;
+  *n = k;
+  return TC_OK;
+}
+
+int tc_plan_free(tc_plan* plan) {
+  if (!plan) return TC_OK;
+  CU(cuCtxSetCurrent)(plan->ctx->cu);
+  if (plan->exec) CU(cuGraphExecDestroy)(plan->exec);
+  if (plan->graph) CU(cuGraphDestroy)(plan->graph);
+  delete plan;
+  return TC_OK;
+}
+
+// ---------------------------------------------------------------- arena planning
+int tc_plan_memory(int n, const uint64_t* bytes, const int32_t* first_use, const int32_t* last_use, uint64_t* offsets,
+                   uint64_t* total) {
+  if (n < 0 || (n && (!bytes || !first_use || !last_use || !offsets)) || !total)
+    return fail(TC_ERR_INVALID, "null argument");
+  std::vector<int> order(n);
+  for (int i = 0; i < n; i++) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return bytes[a] > bytes[b]; });
+  struct Placed { uint64_t off, end; int first, last; };
+  std::vector<Placed> placed;
+  placed.reserve(n);
+  uint64_t top = 0;
+  for (int idx : order) {
+    uint64_t sz = (std::max<uint64_t>(bytes[idx], 1) + 255) / 256 * 256;
+    // candidate offsets: 0 and the end of every placed block whose lifetime overlaps
+    std::vector<std::pair<uint64_t, uint64_t>> busy;
+    for (auto& p : placed)
+      if (!(p.last < first_use[idx] || last_use[idx] < p.first)) busy.push_back({p.off, p.end});
+    std::sort(busy.begin(), busy.end());
+    uint64_t best = UINT64_MAX, best_gap = UINT64_MAX, cur = 0;
+    for (auto& b : busy) {
+      if (b.first > cur && b.first - cur >= sz && b.first - cur < best_gap) { best = cur; best_gap = b.first - cur; }
+      cur = std::max(cur, b.second);
+    }
+    if (best == UINT64_MAX) best = cur;
+    offsets[idx] = best;
+    placed.push_back({best, best + sz, first_use[idx], last_use[idx]});
+    top = std::max(top, best + sz);
+  }
+  *total = top;
+  return TC_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- internal accessors for comm.cpp
+namespace tcb_detail {
+int fail_msg(int status, const std::string& msg) { g_err = msg; return status; }
+CUcontext ctx_of(tc_ctx* ctx) { return ctx->cu; }
+CUstream stream_of(tc_ctx* ctx) { return ctx->stream; }
+}  // namespace tcb_detail

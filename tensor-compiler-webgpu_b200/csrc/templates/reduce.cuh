@@ -1,0 +1,68 @@
+// tcb/reduce.cuh -- the unfused sum/max along one axis (the reference's WGSL
+// form is src/gpu/codegen.js:92-116: one thread per output, serial over n).
+//
+// The input is viewed as [outer, n, inner].  The generated part defines
+// TCB_OUTER, TCB_N, TCB_INNER, TCB_SPLIT (chunks of n), TCB_IS_MAX and then
+// includes this file.
+//  - inner == 1 (last axis): tcb_reduce_rows, a warp per output, coalesced
+//    loads along the row, shuffle tree.
+//  - inner > 1: tcb_reduce_cols, a thread per output column (coalesced across
+//    the warp), serial over its chunk of n.  With TCB_SPLIT > 1 each chunk
+//    writes a partial to scratch ([SPLIT, outer*inner] floats) and
+//    tcb_reduce_finish combines the partials in chunk order.
+#pragma once
+
+namespace tcb {
+__device__ __forceinline__ float red_init() { return TCB_IS_MAX ? -__int_as_float(0x7f800000) : 0.0f; }
+__device__ __forceinline__ float red_comb(float acc, float v) { return TCB_IS_MAX ? op_max(acc, v) : op_add(acc, v); }
+}  // namespace tcb
+
+extern "C" __global__ void __launch_bounds__(256) tcb_reduce_rows(const tcb::Args a) {
+  const float* __restrict__ x = reinterpret_cast<const float*>(a.in[0]);
+  float* __restrict__ out = reinterpret_cast<float*>(a.out);
+  const u64 warp = ((u64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const u64 warps = ((u64)gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  for (u64 o = warp; o < (u64)TCB_OUTER; o += warps) {
+    const float* row = x + o * (u64)TCB_N;
+    float acc = tcb::red_init();
+    for (u64 k = lane; k < (u64)TCB_N; k += 32) acc = tcb::red_comb(acc, __ldg(row + k));
+    acc = TCB_IS_MAX ? tcb::warp_max(acc) : tcb::warp_sum(acc);
+    if (lane == 0) out[o] = acc;
+  }
+}
+
+extern "C" __global__ void __launch_bounds__(256) tcb_reduce_cols(const tcb::Args a) {
+  const float* __restrict__ x = reinterpret_cast<const float*>(a.in[0]);
+  float* __restrict__ dst = TCB_SPLIT > 1 ? reinterpret_cast<float*>(a.scratch) : reinterpret_cast<float*>(a.out);
+  constexpr u64 outs = (u64)TCB_OUTER * (u64)TCB_INNER;
+  constexpr u64 chunk = ((u64)TCB_N + TCB_SPLIT - 1) / TCB_SPLIT;
+  const u64 s = blockIdx.y;
+  const u64 k0 = s * chunk;
+  const u64 k1 = k0 + chunk < (u64)TCB_N ? k0 + chunk : (u64)TCB_N;
+  for (u64 i = (u64)blockIdx.x * blockDim.x + threadIdx.x; i < outs; i += (u64)gridDim.x * blockDim.x) {
+    const u64 o = i / (u64)TCB_INNER, j = i % (u64)TCB_INNER;
+    const float* p = x + (o * (u64)TCB_N) * (u64)TCB_INNER + j;
+    float acc = tcb::red_init();
+    u64 k = k0;
+    for (; k + 4 <= k1; k += 4) {  // four independent loads in flight
+      float v0 = __ldg(p + (k + 0) * (u64)TCB_INNER), v1 = __ldg(p + (k + 1) * (u64)TCB_INNER);
+      float v2 = __ldg(p + (k + 2) * (u64)TCB_INNER), v3 = __ldg(p + (k + 3) * (u64)TCB_INNER);
+      acc = tcb::red_comb(acc, v0); acc = tcb::red_comb(acc, v1);
+      acc = tcb::red_comb(acc, v2); acc = tcb::red_comb(acc, v3);
+    }
+    for (; k < k1; ++k) acc = tcb::red_comb(acc, __ldg(p + k * (u64)TCB_INNER));
+    dst[s * outs + i] = acc;
+  }
+}
+
+extern "C" __global__ void __launch_bounds__(256) tcb_reduce_finish(const tcb::Args a) {
+  const float* __restrict__ part = reinterpret_cast<const float*>(a.scratch);
+  float* __restrict__ out = reinterpret_cast<float*>(a.out);
+  constexpr u64 outs = (u64)TCB_OUTER * (u64)TCB_INNER;
+  for (u64 i = (u64)blockIdx.x * blockDim.x + threadIdx.x; i < outs; i += (u64)gridDim.x * blockDim.x) {
+    float acc = part[i];
+    for (int s = 1; s < TCB_SPLIT; ++s) acc = tcb::red_comb(acc, part[(u64)s * outs + i]);
+    out[i] = acc;
+  }
+}

@@ -1,0 +1,591 @@
+"""The host runtime over libtcb200's C ABI: the replacement of the reference's src/gpu runtime.
+
+* ``GpuRunner``  -- src/gpu/runtime.js:16-130: ``create``, ``info``,
+  ``pipeline(code)`` (compiled once per source text), ``run(graph, lowered,
+  inputs, canary)`` with a buffer per node, optional canary padding and every
+  node read back.
+* ``run_local``  -- src/gpu/harness-m3b.js:86: each launch reads
+  float32-rounded reference operands and writes its own output.
+* ``Program``    -- a lowered graph made resident: one arena planned from
+  buffer lifetimes, every launch resolved into a native plan (tc_plan) that
+  replays without host work or as one CUDA graph.
+* ``GpuTrainer`` / ``FusedTrainer`` -- src/gpu/trainer.js:13-104 and
+  src/fusion/trainer-fused.js:18-109: the persistent training step; each step
+  writes x and y, runs every launch, copies every new parameter and state
+  value into its input buffer on the device, and reads back the loss.
+
+There is no CPU fallback: without the library or a B200 these raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+
+import numpy as np
+
+from . import build as _build
+from .ir import size
+from .codegen import lower, lower_fused, WG
+
+TC_OK = 0
+STATUS = {0: "OK", 1: "INVALID", 2: "CUDA", 3: "COMPILE", 4: "OOM", 5: "TIMEOUT", 6: "NCCL", 7: "UNAVAILABLE"}
+SYNC_TIMEOUT_MS = int(os.environ.get("TCB_SYNC_TIMEOUT_MS", "120000"))
+
+
+class TcError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class Args(ctypes.Structure):
+    _fields_ = [("in_", ctypes.c_uint64 * 8), ("out", ctypes.c_uint64), ("scratch", ctypes.c_uint64),
+                ("p", ctypes.c_int64 * 16)]
+
+
+_lib = None
+
+_SIGS = {
+    "tc_last_error": ([], ctypes.c_char_p),
+    "tc_version": ([], ctypes.c_int),
+    "tc_open": ([ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "tc_close": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_info": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
+    "tc_get_stream": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "tc_set_stream": ([ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
+    "tc_alloc": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "tc_free": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_buf_ptr": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "tc_upload": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "tc_download": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "tc_check_canary": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "tc_memcpy_htod": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
+    "tc_memcpy_dtoh": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "tc_memcpy_dtod": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "tc_memset32": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64], ctypes.c_int),
+    "tc_host_alloc": ([ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "tc_host_free": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_compile": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p,
+                    ctypes.c_size_t], ctypes.c_int),
+    "tc_compile_check": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64)],
+                         ctypes.c_int),
+    "tc_module_free": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_launch": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32),
+                   ctypes.c_uint32, ctypes.POINTER(Args)], ctypes.c_int),
+    "tc_launch_tma": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32),
+                       ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint32, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64),
+                       ctypes.POINTER(Args)], ctypes.c_int),
+    "tc_sync": ([ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
+    "tc_event_create": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "tc_event_record": ([ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
+    "tc_event_elapsed_ms": ([ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_float)], ctypes.c_int),
+    "tc_event_destroy": ([ctypes.c_uint64], ctypes.c_int),
+    "tc_plan_create": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "tc_plan_add_launch": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32),
+                            ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint32, ctypes.POINTER(Args)], ctypes.c_int),
+    "tc_plan_add_launch_tma": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32),
+                                ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint32, ctypes.c_int,
+                                ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(Args)], ctypes.c_int),
+    "tc_plan_add_copy": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "tc_plan_run": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_plan_capture": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_plan_launch_count": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "tc_plan_free": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_plan_memory": ([ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_int32),
+                        ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_uint64),
+                        ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "tc_comm_unique_id": ([ctypes.c_char_p], ctypes.c_int),
+    "tc_comm_init": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
+                      ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "tc_allreduce_f32": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float], ctypes.c_int),
+    "tc_comm_wait": ([ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
+    "tc_comm_abort": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_comm_destroy": ([ctypes.c_void_p], ctypes.c_int),
+}
+
+EXPORTS = tuple(_SIGS)
+
+
+def lib():
+    """The loaded libtcb200.so (built in-tree if missing).  Raises if it cannot be built or loaded."""
+    global _lib
+    if _lib is None:
+        path = _build.LIB
+        if not os.path.exists(path):
+            _build.build()
+        handle = ctypes.CDLL(path)
+        for name, (argtypes, restype) in _SIGS.items():
+            fn = getattr(handle, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = handle
+    return _lib
+
+
+def check(status):
+    if status != TC_OK:
+        raise TcError(status, lib().tc_last_error().decode(errors="replace"))
+
+
+def _u32x3(v):
+    return (ctypes.c_uint32 * 3)(*v)
+
+
+def compile_check(code):
+    """NVRTC-compile `code` for sm_100a without a device; returns the cubin size."""
+    log = ctypes.create_string_buffer(1 << 16)
+    nbytes = ctypes.c_uint64(0)
+    st = lib().tc_compile_check(code.encode(), log, len(log), ctypes.byref(nbytes))
+    if st != TC_OK:
+        raise TcError(st, lib().tc_last_error().decode(errors="replace"))
+    return nbytes.value
+
+
+class Module:
+    __slots__ = ("handle", "runner")
+
+    def __init__(self, handle, runner):
+        self.handle = handle
+        self.runner = runner
+
+
+def make_args(in_ptrs, out_ptr, scratch=0, params=()):
+    a = Args()
+    if len(in_ptrs) > 8:
+        raise ValueError(f"{len(in_ptrs)} operands (at most 8)")
+    for k, p in enumerate(in_ptrs):
+        a.in_[k] = p
+    a.out = out_ptr
+    a.scratch = scratch
+    for k, v in enumerate(params):
+        a.p[k] = int(v)
+    return a
+
+
+class DeviceBuffer:
+    """A device allocation owned by the library (tc_alloc)."""
+    __slots__ = ("handle", "ptr", "nbytes", "runner")
+
+    def __init__(self, runner, nbytes, canary_bytes=0):
+        h = ctypes.c_void_p()
+        check(lib().tc_alloc(runner.ctx, int(nbytes), int(canary_bytes), ctypes.byref(h)))
+        p = ctypes.c_uint64()
+        check(lib().tc_buf_ptr(h, ctypes.byref(p)))
+        self.handle, self.ptr, self.nbytes, self.runner = h, p.value, int(nbytes), runner
+
+    def upload(self, arr, offset=0):
+        a = np.ascontiguousarray(arr)
+        check(lib().tc_upload(self.handle, a.ctypes.data, a.nbytes, offset))
+
+    def download(self, count, dtype=np.float32, offset=0):
+        out = np.empty(count, dtype=dtype)
+        if out.nbytes:
+            check(lib().tc_download(self.handle, out.ctypes.data, out.nbytes, offset))
+        return out
+
+    def canary_intact(self):
+        ok = ctypes.c_int(1)
+        check(lib().tc_check_canary(self.handle, ctypes.byref(ok)))
+        return bool(ok.value)
+
+    def free(self):
+        if self.handle:
+            check(lib().tc_free(self.handle))
+            self.handle = None
+
+
+class GpuRunner:
+    """src/gpu/runtime.js's GpuRunner over libtcb200 (one device, one stream)."""
+
+    def __init__(self, ctx, device):
+        self.ctx = ctx
+        self.device = device
+        self.pipelines = {}
+        self._scratch = None
+        self.lost = None
+
+    @staticmethod
+    def create(device=0):
+        h = ctypes.c_void_p()
+        check(lib().tc_open(device, ctypes.byref(h)))
+        return GpuRunner(h, device)
+
+    def info(self):
+        buf = ctypes.create_string_buffer(4096)
+        check(lib().tc_info(self.ctx, buf, len(buf)))
+        return json.loads(buf.value.decode())
+
+    def pipeline(self, code):
+        """The compiled module for `code`, built once (runtime.js:44-52)."""
+        m = self.pipelines.get(code)
+        if m is None:
+            h = ctypes.c_void_p()
+            log = ctypes.create_string_buffer(1 << 16)
+            check(lib().tc_compile(self.ctx, code.encode(), ctypes.byref(h), log, len(log)))
+            m = self.pipelines[code] = Module(h, self)
+        return m
+
+    def scratch(self, nbytes):
+        if nbytes <= 0:
+            return 0
+        if self._scratch is None or self._scratch.nbytes < nbytes:
+            if self._scratch is not None:
+                self.sync()
+                self._scratch.free()
+            self._scratch = DeviceBuffer(self, nbytes)
+        return self._scratch.ptr
+
+    def stream(self):
+        s = ctypes.c_uint64()
+        check(lib().tc_get_stream(self.ctx, ctypes.byref(s)))
+        return s.value
+
+    def set_stream(self, handle):
+        check(lib().tc_set_stream(self.ctx, int(handle)))
+
+    def sync(self, timeout_ms=SYNC_TIMEOUT_MS):
+        check(lib().tc_sync(self.ctx, int(timeout_ms)))
+
+    def launch(self, lau, in_ptrs, out_ptr):
+        """Issue every kernel call of one Launch (asynchronous)."""
+        mod = self.pipeline(lau.code)
+        scratch = self.scratch(lau.scratch_bytes)
+        for call in lau.calls:
+            args = make_args(in_ptrs, out_ptr, scratch, call.params)
+            check(lib().tc_launch(mod.handle, call.name.encode(), _u32x3(call.grid), _u32x3(call.block),
+                                  call.smem, ctypes.byref(args)))
+
+    def run(self, graph, lowered, inputs, canary=False):
+        """Run `lowered` for `graph`; every node read back (runtime.js:60-129).
+
+        Returns {"values": [float32 arrays per node], "canaryIntact": [bool per node] (with canary)}.
+        """
+        if self.lost:
+            raise TcError(2, f"device lost: {self.lost}")
+        bufs = []
+        try:
+            for node in graph.nodes:
+                n = size(node.shape)
+                pad = ((-(-n // WG)) * WG + WG - n) * 4 if canary else 0
+                bufs.append(DeviceBuffer(self, max(1, n) * 4, pad))
+            for node in graph.nodes:
+                if node.op == "input":
+                    v = np.asarray(inputs[node.attrs["name"]], dtype=np.float32).reshape(-1)
+                    if v.size != size(node.shape):
+                        raise ValueError(f"input '{node.attrs['name']}': expected {size(node.shape)} numbers, got {v.size}")
+                    bufs[node.id].upload(v)
+                elif node.op == "const":
+                    v = node.attrs["value"]
+                    arr = np.full(size(node.shape), v, dtype=np.float32) if isinstance(v, (int, float)) \
+                        else np.asarray(v, dtype=np.float32)
+                    bufs[node.id].upload(arr)
+            for lau in lowered["launches"]:
+                self.launch(lau, [bufs[i].ptr for i in lau.inputs], bufs[lau.node].ptr)
+            self.sync()
+            values = [bufs[node.id].download(size(node.shape)) for node in graph.nodes]
+            intact = [b.canary_intact() for b in bufs] if canary else []
+            return {"values": values, "canaryIntact": intact}
+        finally:
+            for b in bufs:
+                b.free()
+
+    def close(self):
+        if self._scratch is not None:
+            self._scratch.free()
+            self._scratch = None
+        if self.ctx:
+            check(lib().tc_close(self.ctx))
+            self.ctx = None
+
+
+def run_local(runner, graph, lowered, values, canary=False):
+    """Node-local run (src/gpu/harness-m3b.js:86): each launch on float32 reference operands.
+
+    `values` are reference values per node (any float dtype); each launch's
+    operands are uploaded rounded to float32, and its own output is read back.
+    Returns a list with the output of every launched node (None elsewhere).
+    """
+    out = [None] * len(graph.nodes)
+    for lau in lowered["launches"]:
+        bufs = []
+        try:
+            ins = []
+            for i in lau.inputs:
+                b = DeviceBuffer(runner, max(1, size(graph.nodes[i].shape)) * 4)
+                b.upload(np.asarray(values[i], dtype=np.float32).reshape(-1))
+                bufs.append(b)
+                ins.append(b.ptr)
+            n = size(graph.nodes[lau.node].shape)
+            ob = DeviceBuffer(runner, max(1, n) * 4, ((-(-n // WG)) * WG + WG - n) * 4 if canary else 0)
+            bufs.append(ob)
+            runner.launch(lau, ins, ob.ptr)
+            runner.sync()
+            out[lau.node] = ob.download(n)
+            if canary and not ob.canary_intact():
+                raise TcError(1, f"launch for node {lau.node} wrote past its output")
+        finally:
+            for b in bufs:
+                b.free()
+    return out
+
+
+def plan_memory(sizes, first, last):
+    """Arena offsets for buffers with lifetimes [first, last] (tc_plan_memory: best fit, 256-byte aligned)."""
+    n = len(sizes)
+    b = (ctypes.c_uint64 * max(1, n))(*sizes)
+    f = (ctypes.c_int32 * max(1, n))(*first)
+    l_ = (ctypes.c_int32 * max(1, n))(*last)
+    off = (ctypes.c_uint64 * max(1, n))()
+    total = ctypes.c_uint64()
+    check(lib().tc_plan_memory(n, b, f, l_, off, ctypes.byref(total)))
+    return [off[i] for i in range(n)], total.value
+
+
+class Program:
+    """A lowered graph made resident on the device, replayed by a native plan.
+
+    Inputs, constants and `keep` nodes get buffers of their own for the
+    program's life; every other value lives in one arena at an offset planned
+    from its lifetime (producing launch to last consuming launch), so peak
+    memory is the live set, not the graph.  `feedback` pairs (from, to) append
+    device copies after the last launch (the trainers' parameter/state
+    feedback, src/gpu/trainer.js:64).
+    """
+
+    def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False):
+        self.runner = runner
+        self.graph = graph
+        self.launches = lowered["launches"]
+        nodes = graph.nodes
+        self.own = {}
+        keep = set(keep)
+        first = {}
+        last = {}
+        for k, lau in enumerate(self.launches):
+            first[lau.node] = k
+            for i in lau.inputs:
+                last[i] = k
+        arena_ids = []
+        for node in nodes:
+            nbytes = max(1, size(node.shape)) * 4
+            if node.op in ("input", "const") or node.id in keep or node.id not in first:
+                self.own[node.id] = DeviceBuffer(runner, nbytes)
+            else:
+                arena_ids.append(node.id)
+        offs, total = plan_memory([max(1, size(nodes[i].shape)) * 4 for i in arena_ids],
+                                  [first[i] for i in arena_ids], [last.get(i, first[i]) for i in arena_ids])
+        self.arena_bytes = total
+        self.arena = DeviceBuffer(runner, max(total, 256)) if arena_ids else None
+        self.ptrs = {i: b.ptr for i, b in self.own.items()}
+        for i, o in zip(arena_ids, offs):
+            self.ptrs[i] = self.arena.ptr + o
+        for node in nodes:
+            if node.op == "const":
+                v = node.attrs["value"]
+                arr = np.full(size(node.shape), v, dtype=np.float32) if isinstance(v, (int, float)) \
+                    else np.asarray(v, dtype=np.float32)
+                self.own[node.id].upload(arr)
+        scratch_bytes = max([lau.scratch_bytes for lau in self.launches] + [0])
+        self.scratch = DeviceBuffer(runner, scratch_bytes) if scratch_bytes else None
+        h = ctypes.c_void_p()
+        check(lib().tc_plan_create(runner.ctx, ctypes.byref(h)))
+        self.plan = h
+        self.kernel_launches = 0
+        for lau in self.launches:
+            mod = runner.pipeline(lau.code)
+            ins = [self.ptrs[i] for i in lau.inputs]
+            for call in lau.calls:
+                args = make_args(ins, self.ptrs[lau.node], self.scratch.ptr if self.scratch else 0, call.params)
+                check(lib().tc_plan_add_launch(h, mod.handle, call.name.encode(), _u32x3(call.grid),
+                                               _u32x3(call.block), call.smem, ctypes.byref(args)))
+                self.kernel_launches += 1
+        for src, dst in feedback:
+            check(lib().tc_plan_add_copy(h, self.ptrs[dst], self.ptrs[src], max(1, size(nodes[dst].shape)) * 4))
+        self.captured = False
+        if capture:
+            self.capture()
+
+    def capture(self):
+        check(lib().tc_plan_capture(self.plan))
+        self.captured = True
+
+    def ptr(self, nid):
+        return self.ptrs[nid]
+
+    def write(self, nid, arr):
+        """Synchronous upload into node `nid`'s buffer (float32)."""
+        a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).reshape(-1))
+        if a.size != size(self.graph.nodes[nid].shape):
+            raise ValueError(f"node {nid}: {a.size} values for shape {self.graph.nodes[nid].shape}")
+        check(lib().tc_memcpy_htod(self.runner.ctx, self.ptrs[nid], a.ctypes.data, a.nbytes))
+        self.runner.sync()
+
+    def write_async(self, nid, host_ptr, nbytes):
+        check(lib().tc_memcpy_htod(self.runner.ctx, self.ptrs[nid], host_ptr, nbytes))
+
+    def read(self, nid):
+        n = size(self.graph.nodes[nid].shape)
+        out = np.empty(n, dtype=np.float32)
+        self.runner.sync()
+        if n:
+            check(lib().tc_memcpy_dtoh(self.runner.ctx, out.ctypes.data, self.ptrs[nid], out.nbytes))
+        self.runner.sync()
+        return out
+
+    def run(self):
+        check(lib().tc_plan_run(self.plan))
+
+    def free(self):
+        if self.plan:
+            check(lib().tc_plan_free(self.plan))
+            self.plan = None
+        for b in self.own.values():
+            b.free()
+        self.own = {}
+        if self.arena:
+            self.arena.free()
+            self.arena = None
+        if self.scratch:
+            self.scratch.free()
+            self.scratch = None
+
+
+def fused_step(step, sabotage=None, pass_sabotage=None, matmul="naive"):
+    """Fuse a step keeping the loss, logits and every output; ids renumbered (src/fusion/trainer-fused.js:18-29)."""
+    from .fuse import fuse
+    keep = [step["loss"], step["logits"], *step["outputs"].values()]
+    f = fuse(step["graph"], keep=keep, sabotage=pass_sabotage)
+
+    def at(i):
+        return f.index[i]
+    out = dict(step)
+    out.update({"graph": f.graph, "fusion": f, "original": step["graph"], "loss": at(step["loss"]),
+                "logits": at(step["logits"]),
+                "inputs": {k: at(v) for k, v in step["inputs"].items()},
+                "outputs": {k: at(v) for k, v in step["outputs"].items()},
+                "lowered": lower_fused(f.graph, matmul=matmul, sabotage=sabotage)})
+    if "cotangent" in step:
+        out["cotangent"] = step["cotangent"]
+    return out
+
+
+class GpuTrainer:
+    """The persistent training step (src/gpu/trainer.js:13-104; fused: src/fusion/trainer-fused.js:135-213).
+
+    `step` is a builder result (steps.build_mlp_step / build_step3b) or a
+    fused_step() of one.  Parameters and state stay on the device; each
+    train() writes x and y, replays the step (one CUDA graph when `capture`),
+    copies every new parameter/state value into its input and reads the loss.
+    """
+
+    def __init__(self, runner, step, params, state, matmul="naive", sabotage=None, capture=True, lowered=None):
+        self.runner = runner
+        self.step = step
+        graph = step["graph"]
+        if lowered is None:
+            lowered = step.get("lowered") or lower(graph, matmul=matmul, sabotage=sabotage)
+        names = list(params) + list(state)
+        feedback = [(step["outputs"][n], step["inputs"][n]) for n in names]
+        keep = {step["loss"], *[step["outputs"][n] for n in names]}
+        self.prog = Program(runner, graph, lowered, keep=keep, feedback=feedback)
+        cot = graph.input_id(step["cotangent"])
+        if cot is not None:
+            self.prog.write(cot, [1.0])
+        for n, v in {**params, **state}.items():
+            self.prog.write(step["inputs"][n], v)
+        if capture:
+            self.prog.capture()
+
+    def train(self, x, y):
+        """One step on batch (x, y); returns the loss from the parameters before the update."""
+        s = self.step
+        self.prog.write(s["inputs"]["x"], x)
+        self.prog.write(s["inputs"]["y"], y)
+        self.prog.run()
+        return float(self.prog.read(s["loss"])[0])
+
+    def read(self, names):
+        return {n: self.prog.read(self.step["inputs"][n]) for n in names}
+
+    def destroy(self):
+        self.prog.free()
+
+
+class FusedTrainer(GpuTrainer):
+    """GpuTrainer over a fused_step() (its lowering passed in, src/fusion/trainer-fused.js:135-161)."""
+
+    def __init__(self, runner, step, params, state, capture=True):
+        super().__init__(runner, step, params, state, capture=capture, lowered=step["lowered"])
+
+
+class Segments:
+    """Native plans over consecutive launch ranges of a Program, so events can sit between them."""
+
+    def __init__(self, prog, cuts):
+        self.prog = prog
+        self.plans = []
+        bounds = [0, *cuts, len(prog.launches)]
+        for a, b in zip(bounds[:-1], bounds[1:]):
+            h = ctypes.c_void_p()
+            check(lib().tc_plan_create(prog.runner.ctx, ctypes.byref(h)))
+            for lau in prog.launches[a:b]:
+                mod = prog.runner.pipeline(lau.code)
+                ins = [prog.ptrs[i] for i in lau.inputs]
+                for call in lau.calls:
+                    args = make_args(ins, prog.ptrs[lau.node], prog.scratch.ptr if prog.scratch else 0, call.params)
+                    check(lib().tc_plan_add_launch(h, mod.handle, call.name.encode(), _u32x3(call.grid),
+                                                   _u32x3(call.block), call.smem, ctypes.byref(args)))
+            self.plans.append(h)
+
+    def run(self, k):
+        check(lib().tc_plan_run(self.plans[k]))
+
+    def free(self):
+        for h in self.plans:
+            check(lib().tc_plan_free(h))
+        self.plans = []
+
+
+class Events:
+    """CUDA events on the runner's stream."""
+
+    def __init__(self, runner, n):
+        self.runner = runner
+        self.ev = []
+        for _ in range(n):
+            e = ctypes.c_uint64()
+            check(lib().tc_event_create(runner.ctx, ctypes.byref(e)))
+            self.ev.append(e.value)
+
+    def record(self, k):
+        check(lib().tc_event_record(self.runner.ctx, self.ev[k]))
+
+    def ms(self, a, b):
+        v = ctypes.c_float()
+        check(lib().tc_event_elapsed_ms(self.ev[a], self.ev[b], ctypes.byref(v)))
+        return float(v.value)
+
+    def free(self):
+        for e in self.ev:
+            check(lib().tc_event_destroy(e))
+        self.ev = []
+
+
+class PinnedHost:
+    """Page-locked host memory (for the end-to-end path's copies)."""
+
+    def __init__(self, nbytes):
+        p = ctypes.c_void_p()
+        check(lib().tc_host_alloc(int(max(1, nbytes)), ctypes.byref(p)))
+        self.ptr = p.value
+        self.nbytes = int(nbytes)
+
+    def array(self, count, dtype=np.float32):
+        buf = (ctypes.c_char * self.nbytes).from_address(self.ptr)
+        return np.frombuffer(buf, dtype=dtype, count=count)
+
+    def free(self):
+        if self.ptr:
+            check(lib().tc_host_free(self.ptr))
+            self.ptr = None

@@ -28,3 +28,12 @@ def oracle():
     import oracle as o  # noqa: the checker, never the thing measured
     o.build()
     return o
+
+
+@pytest.fixture(scope="session")
+def runner(pkg):
+    """One GPU context for the session.  On a machine without a B200 this errors: there is no CPU fallback."""
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    r = rt.GpuRunner.create(0)
+    yield r
+    r.close()

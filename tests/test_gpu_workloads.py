@@ -1,0 +1,84 @@
+"""The BASELINE workloads on the B200 against the float64 oracle, at sizes the oracle finishes in seconds,
+plus size-independent properties at the full sizes."""
+import importlib
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def wl():
+    return importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+
+
+@pytest.fixture(scope="module")
+def cg():
+    return importlib.import_module("tensor-compiler-webgpu_b200.codegen")
+
+
+def _judge_run(pkg, oracle, runner, cg, graph, inputs, keep, matmul="naive"):
+    values, bounds, rounded = oracle.reference_with_bounds(graph, inputs)
+    fused = pkg.fuse.fuse(graph, keep=keep)
+    gf = runner.run(fused.graph, cg.lower_fused(fused.graph, matmul=matmul), rounded, canary=True)
+    assert all(gf["canaryIntact"])
+    outs = [fused.index[k] for k in keep]
+    j = oracle.judge_outputs([values[k] for k in keep], [bounds[k] for k in keep], [gf["values"][o] for o in outs])
+    return j, fused, gf
+
+
+def test_c1_mlp_forward_backward(pkg, oracle, runner, wl, cg):
+    step = wl.c1_step(64)
+    inputs = wl.c1_inputs(64)
+    inputs[step["cotangent"]] = [1.0]
+    keep = [step["loss"], *step["outputs"].values()]
+    j, _, _ = _judge_run(pkg, oracle, runner, cg, step["graph"], inputs, keep)
+    assert j["pass"], j
+
+
+@pytest.mark.parametrize("R,C", [(64, 8192), (257, 1000)])
+def test_c2_chain_forward_backward(pkg, oracle, runner, wl, cg, R, C):
+    W = wl.c2_graph(R, C)
+    inputs = wl.c2_inputs(W)
+    j, _, _ = _judge_run(pkg, oracle, runner, cg, W["graph"], inputs, W["keep"])
+    assert j["pass"], j
+
+
+@pytest.mark.parametrize("what", ["softmax", "logsoftmax", "rowsum"])
+@pytest.mark.parametrize("R,C", [(300, 4096), (64, 10), (5, 4097)])
+def test_c4_rowwise_forward_backward(pkg, oracle, runner, wl, cg, what, R, C):
+    W = wl.c4_graph(R, C, what)
+    inputs, hot = wl.c4_inputs(W)
+    j, fused, gf = _judge_run(pkg, oracle, runner, cg, W["graph"], inputs, W["keep"])
+    assert j["pass"], j
+    if what == "softmax":  # rows offset by +800 stay finite and sum to 1
+        y = gf["values"][fused.index[W["output"]]].reshape(R, C)
+        assert np.isfinite(y).all()
+        assert np.allclose(y.sum(axis=1), 1.0, atol=1e-4)
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 4096, 128), (130, 1024, 96)])
+@pytest.mark.parametrize("act", ["relu", "tanh"])
+def test_c3_matmul_epilogue(pkg, oracle, runner, wl, cg, M, K, N, act):
+    W = wl.c3_graph(M, K, N, act)
+    inputs = wl.c3_inputs(M, K, N)
+    for matmul in ("naive", "tiled"):
+        j, fused, _ = _judge_run(pkg, oracle, runner, cg, W["graph"], inputs, W["keep"], matmul=matmul)
+        assert [n.attrs["kind"] for n in fused.graph.nodes if n.op == "fused"] == ["epilogue"]
+        assert j["pass"], (matmul, j)
+
+
+def test_transformer_step_small(pkg, oracle, runner, wl, cg):
+    """A C5-shaped step (forward + backward + Adam) at reduced sizes against the oracle."""
+    cfg, c = wl.c5_cfg(d=32, L=1, H=2, ff=64, T=16, batch=2)
+    V = c["V"]
+    s = pkg.steps
+    st = s.build_step3b(V, c["batch"], cfg)
+    params = s.init_params_normal(V, 0, 0.02, cfg)
+    state = s.adam_initial_state(st["names"], s.param_shapes(V, cfg))
+    x, y = wl.one_hot_batch(wl.c5_tokens(c["batch"], cfg["T"], V), V)
+    inputs = {**params, **state, "x": x, "y": y, st["cotangent"]: [1.0]}
+    keep = [st["loss"], st["logits"], *st["outputs"].values()]
+    j, _, _ = _judge_run(pkg, oracle, runner, cg, st["graph"], inputs, keep)
+    assert j["pass"], j
