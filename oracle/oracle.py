@@ -336,3 +336,32 @@ def tensor_score(ours, ref, rtol=1e-12, atol_scale=1e-12):
     r = d / (atol + rtol * np.abs(ref))
     r = np.where(np.isnan(d), np.inf, r)
     return float(r.max())
+
+
+def judge_local(graph, gpu, expected, bound):
+    """Node-local judging with the 1% unjudgeable rule (src/gpu/harness-m4.js:202-223)."""
+    worst, first, unj, elements = 0.0, None, 0, 0
+    by_kind = {}
+    for node in graph.nodes:
+        if expected[node.id] is None:
+            continue
+        r, e = expected[node.id], bound[node.id]
+        g = np.asarray(gpu[node.id], dtype=np.float64).reshape(-1)
+        kind = node.attrs.get("pattern", "plain") if node.op == "fused" else "plain"
+        k = by_kind.setdefault(kind, {"nodes": 0, "worst": 0.0})
+        k["nodes"] += 1
+        bad = ~np.isfinite(r) | (np.abs(r) > F32_MAX) | ~np.isfinite(e)
+        elements += r.size
+        unj += int(bad.sum())
+        ratio = np.where(bad, 0.0, _ratio(g, r, e))
+        if ratio.size:
+            w = float(ratio.max())
+            worst = max(worst, w)
+            k["worst"] = max(k["worst"], w)
+            if w > 1 and first is None:
+                i = int(np.argmax(ratio > 1))
+                first = {"node": node.id, "op": node.op, "pattern": node.attrs.get("pattern"), "index": i,
+                         "gpu": float(g[i]), "ref": float(r[i]), "bound": float(e[i]), "ratio": float(ratio[i])}
+    unjudged = unj > 0.01 * elements
+    return {"pass": first is None and not unjudged, "unjudged": unjudged, "worst": worst, "first": first,
+            "unjudgeable": unj, "elements": elements, "byKind": by_kind}
