@@ -119,15 +119,16 @@ def _barrier(world):
         dist.barrier()
 
 
-def build_workload(name, wl, pkg, cg):
-    """(graph, fused, lowered, inputs, keep, config) for a graph workload at its BASELINE size."""
+def build_workload(name, wl, pkg, cg, rows=None):
+    """(graph, fused, lowered, inputs, keep, config) for a graph workload at its BASELINE size
+    (`rows` cuts C2/C4 to fewer rows: the small case a detailed ncu capture runs on)."""
     if name == "c2":
-        W = wl.c2_graph(8192, 8192)
+        W = wl.c2_graph(rows or 8192, 8192)
         inputs = wl.c2_inputs(W)
         cfg = {"workload": "C2 elementwise chain fp32 [8192,8192] fwd+bwd", "ops": W["ops"],
                "row_broadcast": "[1,8192]", "l2": "operands 256 MiB > 126 MB L2, no flush"}
     elif name == "c4":
-        W = wl.c4_graph(65536, 4096, "softmax")
+        W = wl.c4_graph(rows or 65536, 4096, "softmax")
         inputs, _ = wl.c4_inputs(W)
         cfg = {"workload": "C4 softmax fp32 [65536,4096] fwd+bwd, 1% rows +800", "l2": "1 GiB operands > L2"}
     elif name == "c3":
@@ -192,7 +193,9 @@ def run_ours(args):
         from datetime import timedelta
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    graph, fused, lowered, inputs, keep, cfg, W = build_workload(args.workload, wl, pkg, cg)
+    graph, fused, lowered, inputs, keep, cfg, W = build_workload(args.workload, wl, pkg, cg, args.rows)
+    if args.rows:
+        cfg["workload"] += f" (cut to {args.rows} rows)"
     launches = lowered["launches"]
     step_bytes = sum(l.bytes for l in launches)
     runner = rt.GpuRunner.create(local)
@@ -382,6 +385,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--rows", type=int, default=None, help="cut C2/C4 to fewer rows (profiling cases only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
