@@ -133,6 +133,20 @@ int tc_plan_free(tc_plan* plan);
 int tc_plan_memory(int n, const uint64_t* bytes, const int32_t* first_use, const int32_t* last_use,
                    uint64_t* offsets, uint64_t* total);
 
+/* ---- allocation-free column sum.  No counterpart in the reference: it exists for
+ *      callers that cannot allocate device memory where they need the reduction (inside
+ *      a stream capture, under another allocator's fixed budget, or on a path that
+ *      cannot take cudaMalloc's device-wide synchronisation).
+ *      out[j] = sum over i of in[i * cols + j] (the sum over axis 0 of a row-major
+ *      [rows, cols] float32 matrix), partial sums kept in a library-owned 16 MiB
+ *      static device array (held by every GPU that loads the library until exit).
+ *      cols above 4,194,304 is rejected with TC_ERR_INVALID.  The array is shared by
+ *      all calls and needs no clearing (every partial is written before it is read);
+ *      calls that overlap on the GPU race on it.  The first call on a device looks up
+ *      the array's address with that device current: make it before any stream
+ *      capture.  `stream` is a CUstream / cudaStream_t handle (0 = legacy default). ---- */
+int tc_colsum_f32_static(uint64_t in, uint64_t out, uint64_t rows, uint64_t cols, uint64_t stream);
+
 /* ---- data-parallel collectives (NCCL, loaded at run time) ---- */
 int tc_comm_unique_id(char id[128]);
 int tc_comm_init(tc_ctx* ctx, int rank, int world, const char id[128], int timeout_ms, tc_comm** out);

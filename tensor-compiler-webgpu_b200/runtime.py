@@ -95,6 +95,8 @@ _SIGS = {
     "tc_plan_memory": ([ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_int32),
                         ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_uint64),
                         ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "tc_colsum_f32_static": ([ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64],
+                             ctypes.c_int),
     "tc_comm_unique_id": ([ctypes.c_char_p], ctypes.c_int),
     "tc_comm_init": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
                       ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
