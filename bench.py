@@ -380,7 +380,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c3"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c3", "c5"])
+    ap.add_argument("--batch", type=int, default=None, help="C5 global batch (default 512)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -391,9 +392,142 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c5":
+        run_c5(args)
     else:
         run_ours(args)
 
 
 if __name__ == "__main__":
     main()
+
+
+def run_c5(args):
+    """C5: the decoder transformer's training step, data parallel over the batch (tokens/s)."""
+    world, rank, local = _dist()
+    pkg, rt, cg, wl = _mods()
+    dp = importlib.import_module(PKG + ".dp")
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    cfg, c = wl.c5_cfg(batch=args.batch or wl.C5_CONFIG["batch"])
+    V, B, T = c["V"], c["batch"], cfg["T"]
+    if B % world:
+        raise SystemExit(f"global batch {B} does not split over {world} ranks")
+    bl = B // world
+    runner = rt.GpuRunner.create(local)
+    comm = dp.Comm(runner, rank, world) if world > 1 else None
+    params = pkg.steps.init_params_normal(V, 0, 0.02, cfg)
+    tr = dp.DPTrainer(runner, V, bl, cfg, params, comm=comm, capture=True)
+    toks = wl.c5_tokens(B, T, V, seed=0)[rank * bl:(rank + 1) * bl]
+    x, y = wl.one_hot_batch(toks, V)
+    tr.grad_prog.write(tr.x_id, x)
+    tr.grad_prog.write(tr.y_id, y)
+    K, Wm = args.steps, args.warmup
+    for _ in range(Wm):
+        tr.step_device()
+    runner.sync()
+    if comm:
+        comm.wait()
+    _barrier_gloo(world)
+    ev = rt.Events(runner, 2)
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev.record(0)
+    for _ in range(K):
+        tr.step_device()
+    ev.record(1)
+    runner.sync()
+    if comm:
+        comm.wait()
+    clk = clocks.stop()
+    ms = _max_gloo(ev.ms(0, 1) / K, world)
+    tokens = B * T
+    value = tokens / (ms / 1e3)
+    flops = _matmul_flops(pkg, tr.fg.graph) * world
+    # end to end: this rank's x, y from pinned host memory, the step, the loss back to the host
+    hx, hy = rt.PinnedHost(x.nbytes), rt.PinnedHost(y.nbytes)
+    hx.array(x.size)[:] = x
+    hy.array(y.size)[:] = y
+    hl = rt.PinnedHost(4)
+    lib = rt.lib()
+
+    def e2e():
+        tr.grad_prog.write_async(tr.x_id, hx.ptr, x.nbytes)
+        tr.grad_prog.write_async(tr.y_id, hy.ptr, y.nbytes)
+        tr.step_device()
+        rt.check(lib.tc_memcpy_dtoh(runner.ctx, hl.ptr, tr.grad_prog.ptr(tr.loss_id), 4))
+
+    e2e()
+    runner.sync()
+    ke = max(1, min(K, args.e2e_steps))
+    ev.record(0)
+    for _ in range(ke):
+        e2e()
+    ev.record(1)
+    runner.sync()
+    if comm:
+        comm.wait()
+    e2e_ms = _max_gloo(ev.ms(0, 1) / ke, world)
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": Wm,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic tokens uniform 0..64 (mulberry32 seed 0), weights N(0,0.02)",
+        "config": {"workload": "C5 decoder transformer train step (fwd+bwd+Adam)", "V": V, "d": cfg["d"],
+                   "L": cfg["L"], "H": cfg["H"], "ff": cfg["ff"], "seq_len": T, "global_batch": B,
+                   "parallelism": f"dp{world}", "launches_per_step": tr.kernel_launches,
+                   "arena_bytes": tr.grad_prog.arena_bytes + tr.adam_prog.arena_bytes,
+                   "l2": "activations > L2 (each [B*T, ff] tensor 512 MiB)"},
+        "roofline": {"bound": "tensor", "achieved": round(flops / (ms / 1e3) / 1e12, 2), "peak": None,
+                     "unit": "TFLOP/s", "frac": None, "traffic": None,
+                     "kernel": "whole step: matmul FLOPs / step time (fp32 CUDA-core contractions)"},
+        "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * x.nbytes,
+                "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": K * tr.kernel_launches,
+        "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    for h in (hx, hy, hl):
+        h.free()
+    ev.free()
+    tr.destroy()
+    if comm:
+        comm.destroy()
+    runner.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def _matmul_flops(pkg, graph):
+    flops = 0
+    for n in graph.nodes:
+        if n.op == "fused" and n.attrs["kind"] == "epilogue":
+            b = pkg.fuse.body_of(n)
+            r = next(x for x in b.nodes if x.op == "matmul")
+            a_s, b_s = b.nodes[r.inputs[0]].shape, b.nodes[r.inputs[1]].shape
+        elif n.op == "matmul":
+            a_s, b_s = graph.nodes[n.inputs[0]].shape, graph.nodes[n.inputs[1]].shape
+        else:
+            continue
+        flops += 2 * pkg.ir.size(a_s[:-2]) * a_s[-2] * a_s[-1] * b_s[-1]
+    return flops
+
+
+def _barrier_gloo(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_gloo(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())

@@ -355,7 +355,8 @@ class Program:
     feedback, src/gpu/trainer.js:64).
     """
 
-    def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False):
+    def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False, place=None):
+        """`place` maps node ids to device addresses owned by the caller (e.g. slices of one flat buffer)."""
         self.runner = runner
         self.graph = graph
         self.launches = lowered["launches"]
@@ -369,8 +370,11 @@ class Program:
             for i in lau.inputs:
                 last[i] = k
         arena_ids = []
+        place = place or {}
         for node in nodes:
             nbytes = max(1, size(node.shape)) * 4
+            if node.id in place:
+                continue
             if node.op in ("input", "const") or node.id in keep or node.id not in first:
                 self.own[node.id] = DeviceBuffer(runner, nbytes)
             else:
@@ -380,10 +384,11 @@ class Program:
         self.arena_bytes = total
         self.arena = DeviceBuffer(runner, max(total, 256)) if arena_ids else None
         self.ptrs = {i: b.ptr for i, b in self.own.items()}
+        self.ptrs.update(place)
         for i, o in zip(arena_ids, offs):
             self.ptrs[i] = self.arena.ptr + o
         for node in nodes:
-            if node.op == "const":
+            if node.op == "const" and node.id in self.own:
                 v = node.attrs["value"]
                 arr = np.full(size(node.shape), v, dtype=np.float32) if isinstance(v, (int, float)) \
                     else np.asarray(v, dtype=np.float32)

@@ -1,0 +1,72 @@
+"""The persistent training step on the B200.
+
+* The fused trainer (one native plan, replayed as a CUDA graph, parameters and
+  state fed back on the device) against the checked path -- the same fused
+  launches run one by one through GpuRunner.run with the feedback done on the
+  host -- bit for bit (src/gpu/harness-m4.js:310-330, runConsistencyM4).
+* The data-parallel trainer at world size 1 (gradient graph, Adam graph)
+  against the single fused step graph: the same mathematics partitioned
+  differently, so within float32 tolerance rather than bitwise.
+"""
+import importlib
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_fused_trainer_matches_checked_path_bitwise(pkg, runner):
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    s = pkg.steps
+    step = s.build_mlp_step(wl.C1_DIMS, 64, opt=s.ADAM, hidden="tanh")
+    fstep = rt.fused_step(step)
+    data = wl.c1_inputs(64)
+    params = {k: data[k] for k in s.PARAMS}
+    state = s.mlp_initial_state(s.ADAM, wl.C1_DIMS)
+    tr = rt.FusedTrainer(runner, fstep, params, state)
+    cur = {**{k: np.asarray(v, np.float32) for k, v in params.items()},
+           **{k: np.asarray(v, np.float32) for k, v in state.items()}}
+    names = list(params) + list(state)
+    try:
+        for it in range(3):
+            x = data["x"] if it % 2 == 0 else data["x"][::-1].copy()
+            loss = tr.train(x, data["y"])
+            feed = {**cur, "x": x, "y": data["y"], step["cotangent"]: [1.0]}
+            g = fstep["graph"]
+            out = runner.run(g, fstep["lowered"], {n.attrs["name"]: feed[n.attrs["name"]] for n in g.inputs()})
+            assert np.float32(loss).tobytes() == out["values"][fstep["loss"]].tobytes(), it
+            cur = {k: out["values"][fstep["outputs"][k]] for k in names}
+        got = tr.read(names)
+        for k in names:
+            assert np.array_equal(got[k].view(np.uint32), cur[k].view(np.uint32)), k
+    finally:
+        tr.destroy()
+
+
+def test_dp_trainer_world1_matches_fused_step(pkg, runner):
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    dp = importlib.import_module("tensor-compiler-webgpu_b200.dp")
+    s = pkg.steps
+    cfg, c = wl.c5_cfg(d=64, L=2, H=4, ff=128, T=32, batch=4)
+    V, B = c["V"], c["batch"]
+    params = s.init_params_normal(V, 0, 0.02, cfg)
+    state = s.adam_initial_state(s.param_names(V, cfg), s.param_shapes(V, cfg))
+    x, y = wl.one_hot_batch(wl.c5_tokens(B, cfg["T"], V), V)
+    one = rt.fused_step(s.build_step3b(V, B, cfg))
+    ref = rt.FusedTrainer(runner, one, params, state)
+    tr = dp.DPTrainer(runner, V, B, cfg, params)
+    try:
+        for it in range(3):
+            la = ref.train(x, y)
+            lb = tr.train(x, y)
+            assert abs(la - lb) <= 1e-5 * max(1.0, abs(la)), (it, la, lb)
+        pa = ref.read(tr.names)
+        pb = tr.read(tr.names)
+        for k in tr.names:
+            np.testing.assert_allclose(pb[k], pa[k], rtol=1e-4, atol=1e-6, err_msg=k)
+    finally:
+        ref.destroy()
+        tr.destroy()
