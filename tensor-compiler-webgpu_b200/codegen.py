@@ -541,7 +541,7 @@ def _row_value(em, nid):
 
 
 # ------------------------------------------------------------------ matmul epilogue
-def _epilogue_source(body, out_id, sabotage=None, kernel="simt"):
+def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None):
     root = next(n for n in body.nodes if n.op == "matmul")
     ia, ib = (int(body.nodes[i].attrs["name"][1:]) for i in root.inputs)
     a_s, b_s = body.nodes[root.inputs[0]].shape, body.nodes[root.inputs[1]].shape
@@ -578,6 +578,9 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt"):
         other = next(i for i in bias_add.inputs if i != root.id)
         out = f"tcb::op_add({out}, {em.value(other, base)})"
     code = "\n    ".join(lines)
+    tc_defs = ""
+    if kernel == "tcgen05":
+        tc_defs = (f"#define TCB_KP {_kpad(K)}\n#define TCB_BN {bn}\n#define TCB_STAGES {gemm_stages(bn)}\n")
     src = f"""// matmul epilogue ({kernel}): batch {batch}, [{M},{K}] x [{K},{N}]
 #include "tcb/common.cuh"
 #define TCB_M {M}
@@ -586,16 +589,75 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt"):
 #define TCB_BATCH {batch}
 #define TCB_IA {ia}
 #define TCB_IB {ib}
-struct Epi {{
+{tc_defs}struct Epi {{
   __device__ __forceinline__ static float apply(const tcb::Args& a, float acc, u64 i, u64 row, u64 col, u64 b) {{
     (void)row; (void)col; (void)b;
     {code}
     return {out};
   }}
 }};
-#include "tcb/matmul.cuh"
+#include "tcb/{'gemm_tc' if kernel == 'tcgen05' else 'matmul'}.cuh"
 """
     return src, (batch, M, K, N)
+
+
+# ------------------------------------------------------------------ tensor-core (tcgen05) path
+TC_MIN_K = 32    # below this the 3xTF32 split error could exceed gamma_K's share of the budget: CUDA cores
+GEMM_BM, GEMM_BK = 128, 32
+SMEM_LIMIT = 227 * 1024
+
+
+def _kpad(K):
+    return (K + GEMM_BK - 1) // GEMM_BK * GEMM_BK
+
+
+def gemm_stage_bytes(bn):
+    return 2 * GEMM_BM * GEMM_BK * 4 + 2 * bn * GEMM_BK * 4
+
+
+def gemm_stages(bn):
+    return max(2, min(4, (SMEM_LIMIT - 2048) // gemm_stage_bytes(bn)))
+
+
+def gemm_smem(bn):
+    return gemm_stages(bn) * gemm_stage_bytes(bn) + (2 * gemm_stages(bn) + 1) * 8 + 16 + 1024
+
+
+def gemm_bn(N):
+    """Accumulator width: 256 TMEM columns when N fills them, else 128."""
+    import os
+    forced = os.environ.get("TCB_GEMM_BN")
+    if forced:
+        return int(forced)
+    return 256 if N >= 256 else 128
+
+
+def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage=None):
+    a_s = None
+    root = next(n for n in body.nodes if n.op == "matmul")
+    N = body.nodes[root.inputs[1]].shape[-1]
+    bn = gemm_bn(N)
+    code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage, kernel="tcgen05", bn=bn)
+    if batch > 65535 or math.ceil(M / GEMM_BM) > 65535:
+        raise ValueError("matmul grid too large")
+    Kp = _kpad(K)
+    a_bytes = batch * M * Kp * 4
+    b_bytes = batch * N * Kp * 4
+    err_off = 2 * a_bytes + 2 * b_bytes
+    scratch = err_off + 256
+    maps = [("scratch", 0, Kp, M, batch, Kp * 4, M * Kp * 4, GEMM_BK, GEMM_BM),
+            ("scratch", a_bytes, Kp, M, batch, Kp * 4, M * Kp * 4, GEMM_BK, GEMM_BM),
+            ("scratch", 2 * a_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, GEMM_BK, bn),
+            ("scratch", 2 * a_bytes + b_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, GEMM_BK, bn)]
+    calls = [KernelCall("tcb_split_a", grid1d(batch * M * Kp, per_thread=1), (256, 1, 1)),
+             KernelCall("tcb_split_b", (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)),
+             KernelCall("tcb_gemm_tc", (math.ceil(N / bn), math.ceil(M / GEMM_BM), batch), (192, 1, 1),
+                        gemm_smem(bn), [])]
+    calls[2].tma = maps
+    calls[2].err_offset = err_off
+    lau = Launch(node_id, op, kind, pattern, inputs, code, calls, scratch_bytes=scratch,
+                 info={"mnk": (batch, M, K, N), "bn": bn, "stages": gemm_stages(bn), "path": "tcgen05-3xtf32"})
+    return lau
 
 
 # ------------------------------------------------------------------ plain reduce
@@ -624,11 +686,18 @@ def _reduce_source(op, in_shape, axis):
 
 # ------------------------------------------------------------------ launches
 class KernelCall:
-    """One kernel launch of a Launch: entry name, grid, block, dynamic smem, p[] parameters."""
-    __slots__ = ("name", "grid", "block", "smem", "params")
+    """One kernel launch of a Launch: entry name, grid, block, dynamic smem, p[] parameters.
+
+    ``tma``: tensor maps to build at launch, each (region, offset, cols, rows, batches, row_stride_bytes,
+    batch_stride_bytes, box_cols, box_rows) with region 'scratch'; ``err_offset``: where in scratch the
+    kernel's error word lives (its address goes in p[15]).
+    """
+    __slots__ = ("name", "grid", "block", "smem", "params", "tma", "err_offset")
 
     def __init__(self, name, grid, block, smem=0, params=()):
         self.name, self.grid, self.block, self.smem, self.params = name, tuple(grid), tuple(block), smem, list(params)
+        self.tma = None
+        self.err_offset = None
 
     def __repr__(self):
         return f"KernelCall({self.name}, grid={self.grid}, block={self.block})"
@@ -666,6 +735,10 @@ def _ew_launch(body, out_id, n, kind, node_id, op, pattern, inputs, sabotage=Non
 
 
 def _epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, matmul, sabotage=None):
+    """`matmul`: 'naive' -> the CUDA-core fp32 kernel; 'tiled' -> tcgen05 3xTF32 when K >= TC_MIN_K."""
+    root = next(n for n in body.nodes if n.op == "matmul")
+    if matmul == "tiled" and body.nodes[root.inputs[0]].shape[-1] >= TC_MIN_K:
+        return _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage)
     code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage)
     if batch > 65535:
         raise ValueError("matmul batch above 65535")

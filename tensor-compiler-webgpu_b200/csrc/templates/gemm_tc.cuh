@@ -1,0 +1,268 @@
+// tcb/gemm_tc.cuh -- the matmul epilogue on the 5th-generation tensor cores
+// (class 2 of the fusion pass on its tensor-core path; the reference's WGSL
+// forms are src/gpu/codegen.js:152-193 and src/fusion/codegen-fused.js:176-265).
+//
+// float32 accuracy from TF32 units by the 3xTF32 split: every operand value x
+// is written as hi = rna_tf32(x) and lo = rna_tf32(x - hi), and
+//   A.B ~= A_lo.B_hi + A_hi.B_lo + A_hi.B_hi     (A_lo.B_lo, ~2^-24 |ab|, dropped)
+// accumulated in float32 in tensor memory.  The split is two small kernels
+// (tcb_split_a: A -> A_hi, A_lo; tcb_split_b: B -> B_hi^T, B_lo^T, transposed
+// so both operands are K-major) writing into scratch, zero padded to Kp, a
+// multiple of 32.  The GEMM kernel then:
+//   warp 0   TMA producer: 128-byte-swizzled [rows x 32] fp32 tiles of the four
+//            split operands into a STAGES-deep shared-memory ring (mbarriers);
+//   warp 1   allocates BN TMEM columns, and one lane issues
+//            tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=BN, K=8), 12 per
+//            32-wide k-block, committing each stage back to the producer;
+//   warps 2-5 epilogue: tcgen05.ld of the accumulator rows (warp w reads TMEM
+//            lanes 32*(w%4)..), the fused body (bias, activation, residual ...)
+//            on each value, float4 stores.
+// No TMA multicast.  Every wait is bounded by the global timer; a wait that
+// runs out sets the error word (scratch + err_offset) and the kernel unwinds,
+// freeing its TMEM.
+//
+// The generated part defines TCB_M, TCB_N, TCB_K, TCB_KP, TCB_BATCH, TCB_IA,
+// TCB_IB, TCB_BN, TCB_STAGES and struct Epi (as for tcb/matmul.cuh).
+#pragma once
+
+namespace tcb {
+
+struct alignas(64) TmaDesc { u64 v[16]; };
+struct GemmParams {
+  TmaDesc maps[4];  // A_hi, A_lo, B_hi, B_lo (3-D: {Kp, rows, batch})
+  Args a;
+};
+
+constexpr int GB_M = 128, GB_K = 32;
+constexpr u32 WAIT_NS = 2000000000u;  // 2 s: far above any legitimate wait
+
+__device__ __forceinline__ u32 smem_u32(const void* p) { return (u32)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ u64 now_ns() { u64 t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; }
+
+__device__ __forceinline__ void mbar_init(u32 bar, u32 count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(u32 bar, u32 bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(u32 bar, u32 parity) {
+  u32 ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the error word set) if the barrier phase never completes.
+__device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity, u32* err, u32 code) {
+  if (mbar_try(bar, parity)) return true;
+  const u64 t0 = now_ns();
+  for (u32 it = 0;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 255) == 0 && (now_ns() - t0 > WAIT_NS || (err && *(volatile u32*)err))) {
+      if (err) atomicCAS(err, 0u, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(u32 dst, const TmaDesc* map, u32 bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      :: "r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
+}
+
+// tcgen05 shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart.
+__device__ __forceinline__ u64 sw128_desc(u32 saddr) {
+  u64 d = 0;
+  d |= (u64)((saddr >> 4) & 0x3FFF);        // start address
+  d |= (u64)1 << 16;                         // leading byte offset (unused for swizzled K-major)
+  d |= (u64)(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
+  d |= (u64)1 << 46;                         // descriptor version for sm_100
+  d |= (u64)2 << 61;                         // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = n.
+__host__ __device__ constexpr u32 idesc_tf32(u32 n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((u32)(GB_M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(u32 tmem, u64 a, u64 b, u32 idesc, u32 accumulate) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+               " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}"
+               :: "r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void mma_commit(u32 bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(u32 taddr, float (&r)[16]) {
+  u32 v[16];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                 "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 16; ++j) r[j] = __uint_as_float(v[j]);
+}
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  u32 r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+}  // namespace tcb
+
+// A [batch, M, K] -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.
+extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a) {
+  const float* __restrict__ A = reinterpret_cast<const float*>(a.in[TCB_IA]);
+  float* __restrict__ hi = reinterpret_cast<float*>(a.scratch);
+  float* __restrict__ lo = hi + (u64)TCB_BATCH * TCB_M * TCB_KP;
+  const u64 n = (u64)TCB_BATCH * TCB_M * TCB_KP;
+  for (u64 i = (u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (u64)gridDim.x * blockDim.x) {
+    const u64 k = i % TCB_KP, row = i / TCB_KP;
+    const float x = k < (u64)TCB_K ? __ldg(A + row * TCB_K + k) : 0.0f;
+    const float h = tcb::tf32_rna(x);
+    hi[i] = h;
+    lo[i] = tcb::tf32_rna(x - h);
+  }
+}
+
+// B [batch, K, N] -> B_hi^T, B_lo^T [batch, N, Kp] through 32x32 shared tiles (coalesced both ways).
+extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a) {
+  __shared__ float t[32][33];
+  const float* __restrict__ B = reinterpret_cast<const float*>(a.in[TCB_IB]);
+  float* __restrict__ hi = reinterpret_cast<float*>(a.scratch) + 2ull * TCB_BATCH * TCB_M * TCB_KP;
+  float* __restrict__ lo = hi + (u64)TCB_BATCH * TCB_N * TCB_KP;
+  const u64 b = blockIdx.z;
+  const u64 k0 = (u64)blockIdx.x * 32, n0 = (u64)blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int r = ty; r < 32; r += 8) {
+    const u64 k = k0 + r, nn = n0 + tx;
+    t[r][tx] = (k < (u64)TCB_K && nn < (u64)TCB_N) ? __ldg(B + (b * TCB_K + k) * TCB_N + nn) : 0.0f;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const u64 nn = n0 + r, k = k0 + tx;
+    if (nn < (u64)TCB_N && k < (u64)TCB_KP) {
+      const float x = t[tx][r];
+      const float h = tcb::tf32_rna(x);
+      const u64 o = (b * TCB_N + nn) * TCB_KP + k;
+      hi[o] = h;
+      lo[o] = tcb::tf32_rna(x - h);
+    }
+  }
+}
+
+extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_constant__ tcb::GemmParams P) {
+  using namespace tcb;
+  constexpr int BN = TCB_BN, STAGES = TCB_STAGES;
+  constexpr u32 A_BYTES = GB_M * GB_K * 4, B_BYTES = BN * GB_K * 4;
+  constexpr u32 STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  constexpr u32 KB = TCB_KP / GB_K;
+  extern __shared__ unsigned char smem_raw[];
+  const u32 raw = smem_u32(smem_raw);
+  const u32 base = (raw + 1023u) & ~1023u;
+  unsigned char* gbase = smem_raw + (base - raw);
+  const u32 bars = base + STAGES * STAGE_BYTES;  // full[STAGES], empty[STAGES], accum
+  u32* tmem_slot = reinterpret_cast<u32*>(gbase + STAGES * STAGE_BYTES + (2 * STAGES + 1) * 8);
+  u32* err = reinterpret_cast<u32*>(P.a.p[15]);  // global error word (may be null)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * GB_M, bz = blockIdx.z;
+  auto full = [&](int s) { return bars + 8u * s; };
+  auto empty = [&](int s) { return bars + 8u * (STAGES + s); };
+  const u32 accum = bars + 8u * (2 * STAGES);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(full(s), 1); mbar_init(empty(s), 1); }
+    mbar_init(accum, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(smem_u32(tmem_slot)),
+                 "r"((u32)BN) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const u32 tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (u32 kb = 0; kb < KB; ++kb) {
+        const int s = kb % STAGES;
+        if (kb >= (u32)STAGES && !mbar_wait(empty(s), ((kb / STAGES) - 1) & 1, err, 1)) break;
+        const u32 st = base + s * STAGE_BYTES;
+        mbar_expect_tx(full(s), STAGE_BYTES);
+        const int kc = kb * GB_K;
+        tma_load_3d(st, &P.maps[0], full(s), kc, m0, bz);
+        tma_load_3d(st + A_BYTES, &P.maps[1], full(s), kc, m0, bz);
+        tma_load_3d(st + 2 * A_BYTES, &P.maps[2], full(s), kc, n0, bz);
+        tma_load_3d(st + 2 * A_BYTES + B_BYTES, &P.maps[3], full(s), kc, n0, bz);
+      }
+      // drain: wait (bounded) for the copies still in flight before this CTA may exit
+      for (u32 kb = KB > (u32)STAGES ? KB - STAGES : 0; kb < KB; ++kb)
+        mbar_wait(full(kb % STAGES), (kb / STAGES) & 1, err, 2);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr u32 ID = idesc_tf32(BN);
+      for (u32 kb = 0; kb < KB; ++kb) {
+        const int s = kb % STAGES;
+        if (!mbar_wait(full(s), (kb / STAGES) & 1, err, 3)) break;
+        tc_fence_after();
+        const u32 st = base + s * STAGE_BYTES;
+#pragma unroll
+        for (int k = 0; k < GB_K / 8; ++k) {
+          const u64 ah = sw128_desc(st + 32 * k), al = sw128_desc(st + A_BYTES + 32 * k);
+          const u64 bh = sw128_desc(st + 2 * A_BYTES + 32 * k), bl = sw128_desc(st + 2 * A_BYTES + B_BYTES + 32 * k);
+          mma_tf32(tmem, al, bh, ID, (kb | k) != 0);
+          mma_tf32(tmem, ah, bl, ID, 1);
+          mma_tf32(tmem, ah, bh, ID, 1);
+        }
+        mma_commit(empty(s));
+      }
+      mma_commit(accum);
+    }
+  } else {
+    // epilogue: warps 2..5 -> TMEM lane quarter (warp % 4)
+    const int q = warp & 3;
+    const bool ok = mbar_wait(accum, 0, err, 4);
+    tc_fence_after();
+    const u64 row = (u64)m0 + 32 * q + lane;
+    float* __restrict__ out = reinterpret_cast<float*>(P.a.out);
+    if (ok) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + ((u32)(32 * q) << 16) + (u32)c0, v);
+        if (row < (u64)TCB_M && (u64)(n0 + c0) < (u64)TCB_N) {
+          const u64 base_i = (u64)bz * TCB_M * TCB_N + row * TCB_N + (u64)(n0 + c0);
+          float o[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const u64 col = (u64)(n0 + c0 + j);
+            o[j] = col < (u64)TCB_N ? Epi::apply(P.a, v[j], base_i + j, row, col, (u64)bz) : 0.0f;
+          }
+          if ((TCB_N % 4) == 0 && (u64)(n0 + c0 + 16) <= (u64)TCB_N) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(out + base_i + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+          } else {
+            for (int j = 0; j < 16; ++j) if ((u64)(n0 + c0 + j) < (u64)TCB_N) out[base_i + j] = o[j];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"((u32)BN) : "memory");
+  }
+}

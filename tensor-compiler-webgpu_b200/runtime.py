@@ -152,6 +152,39 @@ class Module:
         self.runner = runner
 
 
+def _map_desc(call, scratch):
+    """The 8-value tensor-map descriptors of a call (include/tcb200.h, tc_launch_tma)."""
+    vals = []
+    for region, off, cols, rows, batches, rs, bs, bc, br in call.tma:
+        if region != "scratch":
+            raise ValueError(f"tensor map over '{region}'")
+        vals += [scratch + off, cols, rows, batches, rs, bs, bc, br]
+    return (ctypes.c_uint64 * len(vals))(*vals)
+
+
+def issue(call, mod, ins, out, scratch, plan=None, ctx=None):
+    """Launch one KernelCall now (plan None) or append it to a native plan."""
+    params = list(call.params)
+    if call.err_offset is not None:
+        while len(params) < 16:
+            params.append(0)
+        params[15] = scratch + call.err_offset
+    args = make_args(ins, out, scratch, params)
+    g, b = _u32x3(call.grid), _u32x3(call.block)
+    if call.tma:
+        desc = _map_desc(call, scratch)
+        if plan is None:
+            check(lib().tc_launch_tma(mod.handle, call.name.encode(), g, b, call.smem, len(call.tma), desc,
+                                      ctypes.byref(args)))
+        else:
+            check(lib().tc_plan_add_launch_tma(plan, mod.handle, call.name.encode(), g, b, call.smem, len(call.tma),
+                                               desc, ctypes.byref(args)))
+    elif plan is None:
+        check(lib().tc_launch(mod.handle, call.name.encode(), g, b, call.smem, ctypes.byref(args)))
+    else:
+        check(lib().tc_plan_add_launch(plan, mod.handle, call.name.encode(), g, b, call.smem, ctypes.byref(args)))
+
+
 def make_args(in_ptrs, out_ptr, scratch=0, params=()):
     a = Args()
     if len(in_ptrs) > 8:
@@ -236,7 +269,19 @@ class GpuRunner:
                 self.sync()
                 self._scratch.free()
             self._scratch = DeviceBuffer(self, nbytes)
+            check(lib().tc_memset32(self.ctx, self._scratch.ptr, 0, nbytes // 4))  # error words start clear
         return self._scratch.ptr
+
+    def check_errors(self, lau, scratch):
+        """A kernel's bounded wait that ran out leaves a nonzero error word: raise it (after a sync)."""
+        for call in lau.calls:
+            if call.err_offset is not None:
+                w = np.zeros(1, np.uint32)
+                check(lib().tc_memcpy_dtoh(self.ctx, w.ctypes.data, scratch + call.err_offset, 4))
+                self.sync()
+                if w[0]:
+                    check(lib().tc_memset32(self.ctx, scratch + call.err_offset, 0, 1))
+                    raise TcError(5, f"{call.name}: a bounded wait ran out (code {int(w[0])})")
 
     def stream(self):
         s = ctypes.c_uint64()
@@ -254,9 +299,8 @@ class GpuRunner:
         mod = self.pipeline(lau.code)
         scratch = self.scratch(lau.scratch_bytes)
         for call in lau.calls:
-            args = make_args(in_ptrs, out_ptr, scratch, call.params)
-            check(lib().tc_launch(mod.handle, call.name.encode(), _u32x3(call.grid), _u32x3(call.block),
-                                  call.smem, ctypes.byref(args)))
+            issue(call, mod, in_ptrs, out_ptr, scratch)
+        return scratch
 
     def run(self, graph, lowered, inputs, canary=False):
         """Run `lowered` for `graph`; every node read back (runtime.js:60-129).
@@ -282,8 +326,12 @@ class GpuRunner:
                     arr = np.full(size(node.shape), v, dtype=np.float32) if isinstance(v, (int, float)) \
                         else np.asarray(v, dtype=np.float32)
                     bufs[node.id].upload(arr)
+            checks = []
             for lau in lowered["launches"]:
-                self.launch(lau, [bufs[i].ptr for i in lau.inputs], bufs[lau.node].ptr)
+                sc = self.launch(lau, [bufs[i].ptr for i in lau.inputs], bufs[lau.node].ptr)
+                if any(c.err_offset is not None for c in lau.calls):
+                    self.sync()
+                    self.check_errors(lau, sc)
             self.sync()
             values = [bufs[node.id].download(size(node.shape)) for node in graph.nodes]
             intact = [b.canary_intact() for b in bufs] if canary else []
@@ -321,8 +369,9 @@ def run_local(runner, graph, lowered, values, canary=False):
             n = size(graph.nodes[lau.node].shape)
             ob = DeviceBuffer(runner, max(1, n) * 4, ((-(-n // WG)) * WG + WG - n) * 4 if canary else 0)
             bufs.append(ob)
-            runner.launch(lau, ins, ob.ptr)
+            sc = runner.launch(lau, ins, ob.ptr)
             runner.sync()
+            runner.check_errors(lau, sc)
             out[lau.node] = ob.download(n)
             if canary and not ob.canary_intact():
                 raise TcError(1, f"launch for node {lau.node} wrote past its output")
@@ -395,6 +444,8 @@ class Program:
                 self.own[node.id].upload(arr)
         scratch_bytes = max([lau.scratch_bytes for lau in self.launches] + [0])
         self.scratch = DeviceBuffer(runner, scratch_bytes) if scratch_bytes else None
+        if self.scratch:
+            check(lib().tc_memset32(runner.ctx, self.scratch.ptr, 0, scratch_bytes // 4))
         h = ctypes.c_void_p()
         check(lib().tc_plan_create(runner.ctx, ctypes.byref(h)))
         self.plan = h
@@ -403,9 +454,7 @@ class Program:
             mod = runner.pipeline(lau.code)
             ins = [self.ptrs[i] for i in lau.inputs]
             for call in lau.calls:
-                args = make_args(ins, self.ptrs[lau.node], self.scratch.ptr if self.scratch else 0, call.params)
-                check(lib().tc_plan_add_launch(h, mod.handle, call.name.encode(), _u32x3(call.grid),
-                                               _u32x3(call.block), call.smem, ctypes.byref(args)))
+                issue(call, mod, ins, self.ptrs[lau.node], self.scratch.ptr if self.scratch else 0, plan=h)
                 self.kernel_launches += 1
         for src, dst in feedback:
             check(lib().tc_plan_add_copy(h, self.ptrs[dst], self.ptrs[src], max(1, size(nodes[dst].shape)) * 4))
@@ -442,6 +491,12 @@ class Program:
 
     def run(self):
         check(lib().tc_plan_run(self.plan))
+
+    def check_errors(self):
+        """Raise if any tensor-core launch's bounded wait ran out (reads the error words after a sync)."""
+        if self.scratch:
+            for lau in self.launches:
+                self.runner.check_errors(lau, self.scratch.ptr)
 
     def free(self):
         if self.plan:
@@ -527,22 +582,23 @@ class FusedTrainer(GpuTrainer):
 
 
 class Segments:
-    """Native plans over consecutive launch ranges of a Program, so events can sit between them."""
+    """Native plans over consecutive kernel-call ranges of a Program, so events can sit between them.
+
+    `cuts` are indices into the flat list of kernel calls (every call of every launch, in order).
+    """
 
     def __init__(self, prog, cuts):
         self.prog = prog
         self.plans = []
-        bounds = [0, *cuts, len(prog.launches)]
+        flat = [(lau, call) for lau in prog.launches for call in lau.calls]
+        bounds = [0, *cuts, len(flat)]
+        scratch = prog.scratch.ptr if prog.scratch else 0
         for a, b in zip(bounds[:-1], bounds[1:]):
             h = ctypes.c_void_p()
             check(lib().tc_plan_create(prog.runner.ctx, ctypes.byref(h)))
-            for lau in prog.launches[a:b]:
+            for lau, call in flat[a:b]:
                 mod = prog.runner.pipeline(lau.code)
-                ins = [prog.ptrs[i] for i in lau.inputs]
-                for call in lau.calls:
-                    args = make_args(ins, prog.ptrs[lau.node], prog.scratch.ptr if prog.scratch else 0, call.params)
-                    check(lib().tc_plan_add_launch(h, mod.handle, call.name.encode(), _u32x3(call.grid),
-                                                   _u32x3(call.block), call.smem, ctypes.byref(args)))
+                issue(call, mod, [prog.ptrs[i] for i in lau.inputs], prog.ptrs[lau.node], scratch, plan=h)
             self.plans.append(h)
 
     def run(self, k):
