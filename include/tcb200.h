@@ -91,6 +91,10 @@ int tc_host_free(void* p);
 int tc_compile(tc_ctx* ctx, const char* cuda_src, tc_module** out, char* log, size_t log_cap);
 /* Compile only (no device needed): NVRTC for sm_100a; *cubin_bytes gets the image size. */
 int tc_compile_check(const char* cuda_src, char* log, size_t log_cap, uint64_t* cubin_bytes);
+/* Compile to a cubin image in caller memory (no device needed); with out == NULL only the size is returned. */
+int tc_compile_cubin(const char* cuda_src, void* out, uint64_t cap, uint64_t* cubin_bytes, char* log, size_t log_cap);
+/* Load a cubin made by tc_compile_cubin (e.g. from an on-disk kernel cache). */
+int tc_module_load(tc_ctx* ctx, const void* cubin, uint64_t bytes, tc_module** out);
 int tc_module_free(tc_module* mod);
 /* One dispatch (runtime.js:86-101's setPipeline/setBindGroup/dispatchWorkgroups). */
 int tc_launch(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],

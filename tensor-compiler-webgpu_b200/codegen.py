@@ -580,7 +580,9 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None):
     code = "\n    ".join(lines)
     tc_defs = ""
     if kernel == "tcgen05":
-        tc_defs = (f"#define TCB_KP {_kpad(K)}\n#define TCB_BN {bn}\n#define TCB_STAGES {gemm_stages(bn)}\n")
+        splitk, part_off = splitk_plan(batch, M, K, N, bn)
+        tc_defs = (f"#define TCB_KP {_kpad(K)}\n#define TCB_BN {bn}\n#define TCB_STAGES {gemm_stages(bn)}\n"
+                   f"#define TCB_SPLITK {splitk}\n#define TCB_PART_OFFSET {part_off}ull\n")
     src = f"""// matmul epilogue ({kernel}): batch {batch}, [{M},{K}] x [{K},{N}]
 #include "tcb/common.cuh"
 #define TCB_M {M}
@@ -623,13 +625,29 @@ def gemm_smem(bn):
     return gemm_stages(bn) * gemm_stage_bytes(bn) + (2 * gemm_stages(bn) + 1) * 8 + 16 + 1024
 
 
+def splitk_plan(batch, M, K, N, bn):
+    """K splits so that short, wide-K contractions (weight gradients) still cover the SMs.
+
+    Returns (splits, byte offset of the partial sums in scratch).  Each split keeps >= 4 k-blocks.
+    """
+    tiles = batch * math.ceil(M / GEMM_BM) * math.ceil(N / bn)
+    kb = _kpad(K) // GEMM_BK
+    s = 1
+    if tiles < SM_COUNT and kb >= 8:
+        s = max(1, min(math.ceil(SM_COUNT / tiles), kb // 4, 64))
+        s = math.ceil(kb / math.ceil(kb / s))  # no empty split
+    Kp = _kpad(K)
+    part_off = 2 * batch * M * Kp * 4 + 2 * batch * N * Kp * 4 + 256
+    return s, part_off
+
+
 def gemm_bn(N):
     """Accumulator width: 256 TMEM columns when N fills them, else 128."""
     import os
     forced = os.environ.get("TCB_GEMM_BN")
     if forced:
         return int(forced)
-    return 256 if N >= 256 else 128
+    return 128
 
 
 def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage=None):
@@ -644,19 +662,26 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
     a_bytes = batch * M * Kp * 4
     b_bytes = batch * N * Kp * 4
     err_off = 2 * a_bytes + 2 * b_bytes
-    scratch = err_off + 256
+    splitk, part_off = splitk_plan(batch, M, K, N, bn)
+    scratch = err_off + 256 + (splitk * batch * M * N * 4 if splitk > 1 else 0)
+    if batch * splitk > 65535:
+        raise ValueError("matmul grid too large")
     maps = [("scratch", 0, Kp, M, batch, Kp * 4, M * Kp * 4, GEMM_BK, GEMM_BM),
             ("scratch", a_bytes, Kp, M, batch, Kp * 4, M * Kp * 4, GEMM_BK, GEMM_BM),
             ("scratch", 2 * a_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, GEMM_BK, bn),
             ("scratch", 2 * a_bytes + b_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, GEMM_BK, bn)]
     calls = [KernelCall("tcb_split_a", grid1d(batch * M * Kp, per_thread=1), (256, 1, 1)),
              KernelCall("tcb_split_b", (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)),
-             KernelCall("tcb_gemm_tc", (math.ceil(N / bn), math.ceil(M / GEMM_BM), batch), (192, 1, 1),
+             KernelCall("tcb_gemm_tc", (math.ceil(N / bn), math.ceil(M / GEMM_BM), batch * splitk), (192, 1, 1),
                         gemm_smem(bn), [])]
+    calls[0].err_offset = err_off
     calls[2].tma = maps
     calls[2].err_offset = err_off
+    if splitk > 1:
+        calls.append(KernelCall("tcb_splitk_finish", grid1d(batch * M * N, per_thread=1), (256, 1, 1)))
     lau = Launch(node_id, op, kind, pattern, inputs, code, calls, scratch_bytes=scratch,
-                 info={"mnk": (batch, M, K, N), "bn": bn, "stages": gemm_stages(bn), "path": "tcgen05-3xtf32"})
+                 info={"mnk": (batch, M, K, N), "bn": bn, "stages": gemm_stages(bn), "splitk": splitk,
+                       "path": "tcgen05-3xtf32"})
     return lau
 
 

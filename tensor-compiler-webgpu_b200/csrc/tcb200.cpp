@@ -408,6 +408,40 @@ int tc_compile_check(const char* src, char* log, size_t log_cap, uint64_t* cubin
   return TC_OK;
 }
 
+int tc_compile_cubin(const char* src, void* out, uint64_t cap, uint64_t* cubin_bytes, char* log, size_t log_cap) {
+  if (!src || !cubin_bytes) return fail(TC_ERR_INVALID, "null argument");
+  std::vector<char> cubin;
+  if (int s = nvrtc_build(src, log, log_cap, &cubin)) return s;
+  *cubin_bytes = cubin.size();
+  if (out) {
+    if (cap < cubin.size()) return fail(TC_ERR_INVALID, "cubin buffer of %llu bytes, need %zu", (unsigned long long)cap,
+                                        cubin.size());
+    memcpy(out, cubin.data(), cubin.size());
+  }
+  return TC_OK;
+}
+
+int tc_module_load(tc_ctx* ctx, const void* cubin, uint64_t bytes, tc_module** out) {
+  if (!cubin || !out || !bytes) return fail(TC_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (int s = bind(ctx)) return s;
+  uint64_t h = fnv1a((const char*)cubin, (size_t)bytes) ^ 0x9e3779b97f4a7c15ull;
+  auto it = ctx->cache.find(h);
+  if (it != ctx->cache.end()) {
+    it->second->refs++;
+    *out = it->second;
+    return TC_OK;
+  }
+  auto mod = std::make_unique<tc_module>();
+  mod->ctx = ctx;
+  CU_TRY(CU(cuModuleLoadData)(&mod->mod, cubin));
+  mod->refs = 2;
+  ctx->cache[h] = mod.get();
+  ctx->cache_src[h] = std::string();
+  *out = mod.release();
+  return TC_OK;
+}
+
 int tc_compile(tc_ctx* ctx, const char* src, tc_module** out, char* log, size_t log_cap) {
   if (!out || !src) return fail(TC_ERR_INVALID, "null argument");
   *out = nullptr;
@@ -415,7 +449,7 @@ int tc_compile(tc_ctx* ctx, const char* src, tc_module** out, char* log, size_t 
   size_t len = strlen(src);
   uint64_t h = fnv1a(src, len);
   auto it = ctx->cache.find(h);
-  if (it != ctx->cache.end() && ctx->cache_src[h] == src) {
+  if (it != ctx->cache.end() && !ctx->cache_src[h].empty() && ctx->cache_src[h] == src) {
     it->second->refs++;
     *out = it->second;
     return TC_OK;

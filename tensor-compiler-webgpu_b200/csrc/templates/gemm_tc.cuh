@@ -116,8 +116,14 @@ __device__ __forceinline__ float tf32_rna(float x) {
 
 }  // namespace tcb
 
-// A [batch, M, K] -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.
+#ifndef TCB_SPLITK
+#define TCB_SPLITK 1
+#endif
+
+// A [batch, M, K] -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.  It runs first in every
+// tensor-core launch, so it also clears that launch's error word (p[15]) in the reused scratch.
 extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a) {
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.p[15]) *reinterpret_cast<u32*>(a.p[15]) = 0u;
   const float* __restrict__ A = reinterpret_cast<const float*>(a.in[TCB_IA]);
   float* __restrict__ hi = reinterpret_cast<float*>(a.scratch);
   float* __restrict__ lo = hi + (u64)TCB_BATCH * TCB_M * TCB_KP;
@@ -162,7 +168,8 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
   constexpr int BN = TCB_BN, STAGES = TCB_STAGES;
   constexpr u32 A_BYTES = GB_M * GB_K * 4, B_BYTES = BN * GB_K * 4;
   constexpr u32 STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-  constexpr u32 KB = TCB_KP / GB_K;
+  constexpr u32 KB_ALL = TCB_KP / GB_K;
+  constexpr u32 KB_PER = (KB_ALL + TCB_SPLITK - 1) / TCB_SPLITK;  // k-blocks per split
   extern __shared__ unsigned char smem_raw[];
   const u32 raw = smem_u32(smem_raw);
   const u32 base = (raw + 1023u) & ~1023u;
@@ -172,7 +179,11 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
   u32* err = reinterpret_cast<u32*>(P.a.p[15]);  // global error word (may be null)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * GB_M, bz = blockIdx.z;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * GB_M, bz = blockIdx.z / TCB_SPLITK;
+  const u32 split = blockIdx.z % TCB_SPLITK;
+  const u32 kb_begin = split * KB_PER;
+  const u32 kb_end = kb_begin + KB_PER < KB_ALL ? kb_begin + KB_PER : KB_ALL;
+  const u32 KB = kb_end > kb_begin ? kb_end - kb_begin : 0;
   auto full = [&](int s) { return bars + 8u * s; };
   auto empty = [&](int s) { return bars + 8u * (STAGES + s); };
   const u32 accum = bars + 8u * (2 * STAGES);
@@ -199,7 +210,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
         if (kb >= (u32)STAGES && !mbar_wait(empty(s), ((kb / STAGES) - 1) & 1, err, 1)) break;
         const u32 st = base + s * STAGE_BYTES;
         mbar_expect_tx(full(s), STAGE_BYTES);
-        const int kc = kb * GB_K;
+        const int kc = (kb_begin + kb) * GB_K;
         tma_load_3d(st, &P.maps[0], full(s), kc, m0, bz);
         tma_load_3d(st + A_BYTES, &P.maps[1], full(s), kc, m0, bz);
         tma_load_3d(st + 2 * A_BYTES, &P.maps[2], full(s), kc, n0, bz);
@@ -227,7 +238,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
         }
         mma_commit(empty(s));
       }
-      mma_commit(accum);
+      mma_commit(accum);  // with no k-block in this split the accumulator is never enabled: see the epilogue
     }
   } else {
     // epilogue: warps 2..5 -> TMEM lane quarter (warp % 4)
@@ -241,6 +252,20 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         tmem_ld16(tmem + ((u32)(32 * q) << 16) + (u32)c0, v);
+        if (KB == 0) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+        }
+        if (TCB_SPLITK > 1) {
+          // partial sums of this split: [SPLITK][batch][M][N] floats after the split operands in scratch
+          if (row < (u64)TCB_M) {
+            float* part = reinterpret_cast<float*>(P.a.scratch) + TCB_PART_OFFSET / 4 +
+                          (((u64)split * TCB_BATCH + bz) * TCB_M + row) * TCB_N;
+            for (int j = 0; j < 16; ++j)
+              if ((u64)(n0 + c0 + j) < (u64)TCB_N) part[n0 + c0 + j] = v[j];
+          }
+          continue;
+        }
         if (row < (u64)TCB_M && (u64)(n0 + c0) < (u64)TCB_N) {
           const u64 base_i = (u64)bz * TCB_M * TCB_N + row * TCB_N + (u64)(n0 + c0);
           float o[16];
@@ -265,4 +290,19 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"((u32)BN) : "memory");
   }
+}
+
+// Split-K: out = Epi(sum over splits s = 0.. of partial[s]), in split order (deterministic).
+extern "C" __global__ void __launch_bounds__(256) tcb_splitk_finish(const tcb::Args a) {
+#if TCB_SPLITK > 1
+  const float* __restrict__ part = reinterpret_cast<const float*>(a.scratch) + TCB_PART_OFFSET / 4;
+  float* __restrict__ out = reinterpret_cast<float*>(a.out);
+  constexpr u64 n = (u64)TCB_BATCH * TCB_M * TCB_N;
+  for (u64 i = (u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (u64)gridDim.x * blockDim.x) {
+    float acc = part[i];
+    for (int s = 1; s < TCB_SPLITK; ++s) acc = tcb::op_add(acc, part[(u64)s * n + i]);
+    const u64 col = i % TCB_N, row = (i / TCB_N) % TCB_M, b = i / ((u64)TCB_M * TCB_N);
+    out[i] = Epi::apply(a, acc, i, row, col, b);
+  }
+#endif
 }

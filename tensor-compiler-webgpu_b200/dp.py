@@ -64,7 +64,7 @@ class DPTrainer:
     """The transformer training step, data parallel.  `batch_local` sequences per rank."""
 
     def __init__(self, runner, V, batch_local, cfg, params, state=None, comm=None, opt=_steps.ADAM_3B,
-                 matmul="naive", capture=True):
+                 matmul="tiled", capture=True):
         self.runner, self.comm = runner, comm
         gs = _steps.build_grad3b(V, batch_local, cfg)
         ad = _steps.build_adam_graph(V, cfg, opt)

@@ -70,6 +70,10 @@ _SIGS = {
                     ctypes.c_size_t], ctypes.c_int),
     "tc_compile_check": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64)],
                          ctypes.c_int),
+    "tc_compile_cubin": ([ctypes.c_char_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64),
+                          ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
+    "tc_module_load": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)],
+                       ctypes.c_int),
     "tc_module_free": ([ctypes.c_void_p], ctypes.c_int),
     "tc_launch": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32),
                    ctypes.c_uint32, ctypes.POINTER(Args)], ctypes.c_int),
@@ -142,6 +146,49 @@ def compile_check(code):
     if st != TC_OK:
         raise TcError(st, lib().tc_last_error().decode(errors="replace"))
     return nbytes.value
+
+
+CACHE_DIR = os.environ.get("TCB_KERNEL_CACHE", os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                               "_kernel_cache"))
+
+
+def _cache_path(code):
+    import hashlib
+    return os.path.join(CACHE_DIR, hashlib.sha256(code.encode()).hexdigest()[:32] + ".cubin")
+
+
+def compile_cubin(code):
+    """NVRTC cubin for `code` (sm_100a), from the on-disk kernel cache when present; no device needed."""
+    path = _cache_path(code)
+    if os.path.exists(path):
+        with open(path, "rb") as f:
+            return f.read()
+    n = ctypes.c_uint64(0)
+    log = ctypes.create_string_buffer(1 << 16)
+    check(lib().tc_compile_cubin(code.encode(), None, 0, ctypes.byref(n), log, len(log)))
+    buf = ctypes.create_string_buffer(n.value)
+    check(lib().tc_compile_cubin(code.encode(), buf, n.value, ctypes.byref(n), log, len(log)))
+    data = buf.raw[:n.value]
+    try:
+        os.makedirs(CACHE_DIR, exist_ok=True)
+        tmp = f"{path}.{os.getpid()}.tmp"
+        with open(tmp, "wb") as f:
+            f.write(data)
+        os.replace(tmp, path)
+    except OSError:
+        pass
+    return data
+
+
+def precompile(codes, threads=None):
+    """Compile many sources in parallel threads into the kernel cache (ctypes releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+    todo = sorted({c for c in codes if not os.path.exists(_cache_path(c))})
+    if not todo:
+        return 0
+    with ThreadPoolExecutor(threads or min(16, os.cpu_count() or 4)) as ex:
+        list(ex.map(compile_cubin, todo))
+    return len(todo)
 
 
 class Module:
@@ -255,9 +302,9 @@ class GpuRunner:
         """The compiled module for `code`, built once (runtime.js:44-52)."""
         m = self.pipelines.get(code)
         if m is None:
+            cubin = compile_cubin(code)
             h = ctypes.c_void_p()
-            log = ctypes.create_string_buffer(1 << 16)
-            check(lib().tc_compile(self.ctx, code.encode(), ctypes.byref(h), log, len(log)))
+            check(lib().tc_module_load(self.ctx, cubin, len(cubin), ctypes.byref(h)))
             m = self.pipelines[code] = Module(h, self)
         return m
 

@@ -1,0 +1,61 @@
+"""Fill the on-disk kernel cache for the standard workloads (NVRTC, no GPU needed).
+
+Every fused node is its own NVRTC instantiation, so a cold process spends
+seconds compiling; build() runs this once so the benches, tests and smoke
+load cubins instead.  The cache is keyed by a hash of each kernel's full
+source, so a changed template or body simply misses.
+"""
+from __future__ import annotations
+
+from . import codegen as cg
+from . import runtime as rt
+from . import workloads as wl
+from .fuse import fuse
+from . import steps as _steps
+from .cases import fused_direct_cases
+
+
+def _codes(graph, keep=(), matmul="naive"):
+    f = fuse(graph, keep=list(keep))
+    return {lau.code for lau in cg.lower_fused(f.graph, matmul=matmul)["launches"]} | \
+        {lau.code for lau in cg.lower(graph, matmul=matmul)["launches"]}
+
+
+def standard_sources(full=True):
+    codes = set()
+    for c in fused_direct_cases():
+        codes |= _codes(c["graph"], matmul=c.get("matmul", "naive"))
+    W = wl.c2_graph(256, 1024)
+    codes |= _codes(W["graph"], W["keep"])
+    for R, C in ((64, 8192), (257, 1000)):
+        W = wl.c2_graph(R, C)
+        codes |= _codes(W["graph"], W["keep"])
+    for what in ("softmax", "logsoftmax", "rowsum"):
+        for R, C in ((300, 4096), (64, 10), (5, 4097)):
+            W = wl.c4_graph(R, C, what)
+            codes |= _codes(W["graph"], W["keep"])
+    for M, K, N in ((256, 4096, 128), (130, 1024, 96)):
+        for act in ("relu", "tanh"):
+            W = wl.c3_graph(M, K, N, act)
+            codes |= _codes(W["graph"], W["keep"], "naive") | _codes(W["graph"], W["keep"], "tiled")
+    step = wl.c1_step(64)
+    codes |= _codes(step["graph"], [step["loss"], *step["outputs"].values()])
+    if full:
+        W = wl.c2_graph(8192, 8192)
+        codes |= _codes(W["graph"], W["keep"])
+        W = wl.c4_graph(65536, 4096, "softmax")
+        codes |= _codes(W["graph"], W["keep"])
+        W = wl.c3_graph(4096, 4096, 4096, "relu")
+        codes |= _codes(W["graph"], W["keep"], "tiled")
+        cfg, c = wl.c5_cfg()
+        gs = _steps.build_grad3b(c["V"], c["batch"], cfg)
+        f = fuse(gs["graph"], keep=[gs["loss"], *gs["grads"].values()])
+        codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul="tiled")["launches"]}
+        ad = _steps.build_adam_graph(c["V"], cfg)
+        fa = fuse(ad["graph"], keep=list(ad["outputs"].values()))
+        codes |= {lau.code for lau in cg.lower_fused(fa.graph, matmul="tiled")["launches"]}
+    return codes
+
+
+def warm(full=True):
+    return rt.precompile(standard_sources(full))
