@@ -670,7 +670,7 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
             ("scratch", a_bytes, Kp, M, batch, Kp * 4, M * Kp * 4, GEMM_BK, GEMM_BM),
             ("scratch", 2 * a_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, GEMM_BK, bn),
             ("scratch", 2 * a_bytes + b_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, GEMM_BK, bn)]
-    calls = [KernelCall("tcb_split_a", grid1d(batch * M * Kp, per_thread=1), (256, 1, 1)),
+    calls = [KernelCall("tcb_split_a", grid1d(batch * M * Kp, per_thread=4), (256, 1, 1)),
              KernelCall("tcb_split_b", (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)),
              KernelCall("tcb_gemm_tc", (math.ceil(N / bn), math.ceil(M / GEMM_BM), batch * splitk), (192, 1, 1),
                         gemm_smem(bn), [])]

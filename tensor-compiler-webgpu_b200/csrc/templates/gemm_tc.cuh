@@ -122,18 +122,29 @@ __device__ __forceinline__ float tf32_rna(float x) {
 
 // A [batch, M, K] -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.  It runs first in every
 // tensor-core launch, so it also clears that launch's error word (p[15]) in the reused scratch.
+// Four elements per thread step: 128-bit stores always (Kp % 32 == 0), 128-bit loads when K % 4 == 0.
 extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a) {
   if (blockIdx.x == 0 && threadIdx.x == 0 && a.p[15]) *reinterpret_cast<u32*>(a.p[15]) = 0u;
   const float* __restrict__ A = reinterpret_cast<const float*>(a.in[TCB_IA]);
   float* __restrict__ hi = reinterpret_cast<float*>(a.scratch);
   float* __restrict__ lo = hi + (u64)TCB_BATCH * TCB_M * TCB_KP;
-  const u64 n = (u64)TCB_BATCH * TCB_M * TCB_KP;
-  for (u64 i = (u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (u64)gridDim.x * blockDim.x) {
+  constexpr u64 n4 = (u64)TCB_BATCH * TCB_M * TCB_KP / 4;
+  for (u64 v = (u64)blockIdx.x * blockDim.x + threadIdx.x; v < n4; v += (u64)gridDim.x * blockDim.x) {
+    const u64 i = v * 4;
     const u64 k = i % TCB_KP, row = i / TCB_KP;
-    const float x = k < (u64)TCB_K ? __ldg(A + row * TCB_K + k) : 0.0f;
-    const float h = tcb::tf32_rna(x);
-    hi[i] = h;
-    lo[i] = tcb::tf32_rna(x - h);
+    float x[4];
+    if ((TCB_K % 4) == 0 && k + 4 <= (u64)TCB_K) {
+      const float4 q = __ldg(reinterpret_cast<const float4*>(A + row * TCB_K + k));
+      x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[j] = (k + j < (u64)TCB_K) ? __ldg(A + row * TCB_K + k + j) : 0.0f;
+    }
+    float h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { h[j] = tcb::tf32_rna(x[j]); l[j] = tcb::tf32_rna(x[j] - h[j]); }
+    *reinterpret_cast<float4*>(hi + i) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo + i) = make_float4(l[0], l[1], l[2], l[3]);
   }
 }
 

@@ -55,9 +55,9 @@ def test_dp_trainer_world1_matches_fused_step(pkg, runner):
     params = s.init_params_normal(V, 0, 0.02, cfg)
     state = s.adam_initial_state(s.param_names(V, cfg), s.param_shapes(V, cfg))
     x, y = wl.one_hot_batch(wl.c5_tokens(B, cfg["T"], V), V)
-    one = rt.fused_step(s.build_step3b(V, B, cfg))
+    one = rt.fused_step(s.build_step3b(V, B, cfg), matmul="tiled")
     ref = rt.FusedTrainer(runner, one, params, state)
-    tr = dp.DPTrainer(runner, V, B, cfg, params)
+    tr = dp.DPTrainer(runner, V, B, cfg, params, matmul="tiled")
     try:
         for it in range(3):
             la = ref.train(x, y)
