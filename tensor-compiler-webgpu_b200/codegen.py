@@ -541,7 +541,7 @@ def _row_value(em, nid):
 
 
 # ------------------------------------------------------------------ matmul epilogue
-def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None):
+def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=False, b_t=False):
     root = next(n for n in body.nodes if n.op == "matmul")
     ia, ib = (int(body.nodes[i].attrs["name"][1:]) for i in root.inputs)
     a_s, b_s = body.nodes[root.inputs[0]].shape, body.nodes[root.inputs[1]].shape
@@ -582,7 +582,8 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None):
     if kernel == "tcgen05":
         splitk, part_off = splitk_plan(batch, M, K, N, bn)
         tc_defs = (f"#define TCB_KP {_kpad(K)}\n#define TCB_BN {bn}\n#define TCB_STAGES {gemm_stages(bn)}\n"
-                   f"#define TCB_SPLITK {splitk}\n#define TCB_PART_OFFSET {part_off}ull\n")
+                   f"#define TCB_SPLITK {splitk}\n#define TCB_PART_OFFSET {part_off}ull\n"
+                   f"#define TCB_A_T {int(a_t)}\n#define TCB_B_T {int(b_t)}\n")
     src = f"""// matmul epilogue ({kernel}): batch {batch}, [{M},{K}] x [{K},{N}]
 #include "tcb/common.cuh"
 #define TCB_M {M}
@@ -650,12 +651,11 @@ def gemm_bn(N):
     return 128
 
 
-def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage=None):
-    a_s = None
+def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage=None, a_t=False, b_t=False):
     root = next(n for n in body.nodes if n.op == "matmul")
     N = body.nodes[root.inputs[1]].shape[-1]
     bn = gemm_bn(N)
-    code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage, kernel="tcgen05", bn=bn)
+    code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage, kernel="tcgen05", bn=bn, a_t=a_t, b_t=b_t)
     if batch > 65535 or math.ceil(M / GEMM_BM) > 65535:
         raise ValueError("matmul grid too large")
     Kp = _kpad(K)
@@ -670,8 +670,10 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
             ("scratch", a_bytes, Kp, M, batch, Kp * 4, M * Kp * 4, GEMM_BK, GEMM_BM),
             ("scratch", 2 * a_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, GEMM_BK, bn),
             ("scratch", 2 * a_bytes + b_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, GEMM_BK, bn)]
-    calls = [KernelCall("tcb_split_a", grid1d(batch * M * Kp, per_thread=4), (256, 1, 1)),
-             KernelCall("tcb_split_b", (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)),
+    calls = [KernelCall("tcb_split_a", (Kp // 32, math.ceil(M / 32), batch) if a_t
+                        else grid1d(batch * M * Kp, per_thread=4), (256, 1, 1)),
+             KernelCall("tcb_split_b", grid1d(batch * N * Kp, per_thread=4) if b_t
+                        else (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)),
              KernelCall("tcb_gemm_tc", (math.ceil(N / bn), math.ceil(M / GEMM_BM), batch * splitk), (192, 1, 1),
                         gemm_smem(bn), [])]
     calls[0].err_offset = err_off
@@ -681,7 +683,7 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
         calls.append(KernelCall("tcb_splitk_finish", grid1d(batch * M * N, per_thread=1), (256, 1, 1)))
     lau = Launch(node_id, op, kind, pattern, inputs, code, calls, scratch_bytes=scratch,
                  info={"mnk": (batch, M, K, N), "bn": bn, "stages": gemm_stages(bn), "splitk": splitk,
-                       "path": "tcgen05-3xtf32"})
+                       "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t})
     return lau
 
 
@@ -759,11 +761,20 @@ def _ew_launch(body, out_id, n, kind, node_id, op, pattern, inputs, sabotage=Non
     return Launch(node_id, op, kind, pattern, inputs, code, [call])
 
 
-def _epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, matmul, sabotage=None):
-    """`matmul`: 'naive' -> the CUDA-core fp32 kernel; 'tiled' -> tcgen05 3xTF32 when K >= TC_MIN_K."""
+def uses_tensor_cores(a_shape, matmul):
+    return matmul == "tiled" and a_shape[-1] >= TC_MIN_K
+
+
+def _epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, matmul, sabotage=None, a_t=False, b_t=False):
+    """`matmul`: 'naive' -> the CUDA-core fp32 kernel; 'tiled' -> tcgen05 3xTF32 when K >= TC_MIN_K.
+
+    `a_t` / `b_t`: the operand's slot holds its transpose (a folded transposeLast2, tensor-core path only).
+    """
     root = next(n for n in body.nodes if n.op == "matmul")
-    if matmul == "tiled" and body.nodes[root.inputs[0]].shape[-1] >= TC_MIN_K:
-        return _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage)
+    if uses_tensor_cores(body.nodes[root.inputs[0]].shape, matmul):
+        return _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage, a_t, b_t)
+    if a_t or b_t:
+        raise ValueError("transposed operands are folded only on the tensor-core path")
     code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage)
     if batch > 65535:
         raise ValueError("matmul batch above 65535")
@@ -842,16 +853,87 @@ def _bytes(graph, lau):
     return b + size(graph.nodes[lau.node].shape) * 4
 
 
-def lower(graph, matmul="naive", sabotage=None):
-    """One launch per op, no fusion (src/gpu/lower.js:68-114)."""
+def _is_last2_swap(node):
+    p = node.attrs.get("perm")
+    r = len(p)
+    return r >= 2 and p[:-2] == list(range(r - 2)) and p[-2:] == [r - 1, r - 2]
+
+
+def _matmul_operands(graph, node):
+    """(node of the contraction's A, node of its B) as graph ids, for a plain matmul or an epilogue node."""
+    if node.op == "matmul":
+        return node.inputs[0], node.inputs[1]
+    if node.op == "fused" and node.attrs["kind"] == "epilogue":
+        from .fuse import body_of
+        b = body_of(node)
+        root = next(n for n in b.nodes if n.op == "matmul")
+        ia, ib = (int(b.nodes[i].attrs["name"][1:]) for i in root.inputs)
+        # an operand slot used anywhere else in the body is read at output indices: not foldable
+        uses = {}
+        for n in b.nodes:
+            for i in n.inputs:
+                uses[i] = uses.get(i, 0) + 1
+        if uses.get(root.inputs[0], 0) != 1 or uses.get(root.inputs[1], 0) != 1 or root.inputs[0] == root.inputs[1]:
+            return None
+        return node.inputs[ia], node.inputs[ib]
+    return None
+
+
+def foldable_transposes(graph, matmul, keep=()):
+    """Plain transposeLast2 nodes read only as tensor-core GEMM operands: their launch can be dropped and the
+    GEMM's operand split reads the transpose's source instead (the split rewrites the layout anyway)."""
+    keep = set(keep)
+    consumers = {}
+    for n in graph.nodes:
+        for i in n.inputs:
+            consumers.setdefault(i, []).append(n)
+    folds = set()
+    for t in graph.nodes:
+        if t.op != "transpose" or t.id in keep or not _is_last2_swap(t) or t.id not in consumers:
+            continue
+        ok = True
+        for c in consumers[t.id]:
+            ops = _matmul_operands(graph, c)
+            if ops is None or t.id not in ops or not uses_tensor_cores(graph.nodes[ops[0]].shape, matmul):
+                ok = False
+                break
+        if ok:
+            folds.add(t.id)
+    return folds
+
+
+def _folded_launch(graph, node, matmul, sabotage, folds):
+    """The GEMM launch of `node` with folded transposed operands substituted by their sources."""
+    from .fuse import body_of
+    a, b = _matmul_operands(graph, node)
+    a_t, b_t = a in folds, b in folds
+    if node.op == "matmul":
+        shapes = [list(graph.nodes[i].shape) for i in node.inputs]
+        body, out = _one_op_body("matmul", shapes, node.attrs)
+        lau = _epilogue_launch(body, out, node.id, "matmul", f"matmul-{matmul}", None, list(node.inputs), matmul,
+                               None, a_t, b_t)
+    else:
+        lau = _epilogue_launch(body_of(node), node.attrs["output"], node.id, "fused", "fused-epilogue",
+                               node.attrs["pattern"], list(node.inputs), matmul,
+                               sabotage if sabotage in FUSED_SABOTAGE else None, a_t, b_t)
+    lau.inputs = [graph.nodes[i].inputs[0] if i in folds else i for i in node.inputs]
+    return lau
+
+
+def lower(graph, matmul="naive", sabotage=None, fold=False, keep=()):
+    """One launch per op, no fusion (src/gpu/lower.js:68-114).  `fold`: drop transposes feeding GEMM operands."""
+    folds = foldable_transposes(graph, matmul, keep) if fold else set()
     launches = []
     for node in graph.nodes:
-        if node.op in ("input", "const"):
+        if node.op in ("input", "const") or node.id in folds:
             continue
-        lau = _plain_launch(graph, node, matmul)
+        if folds and _matmul_operands(graph, node) and set(_matmul_operands(graph, node)) & folds:
+            lau = _folded_launch(graph, node, matmul, sabotage, folds)
+        else:
+            lau = _plain_launch(graph, node, matmul)
         lau.bytes = _bytes(graph, lau)
         launches.append(lau)
-    return {"launches": launches}
+    return {"launches": launches, "folded": sorted(folds)}
 
 
 def fused_kernel(node, matmul="naive", sabotage=None):
@@ -872,16 +954,25 @@ def fused_kernel(node, matmul="naive", sabotage=None):
     raise ValueError(f"no fused kernel kind '{kind}'")
 
 
-def lower_fused(graph, matmul="naive", sabotage=None):
-    """A fused node to its kernel, every other node to its plain launch (src/fusion/lower-fused.js:32-45)."""
+def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=()):
+    """A fused node to its kernel, every other node to its plain launch (src/fusion/lower-fused.js:32-45).
+
+    `fold` (resident programs only): transposeLast2 nodes read only as tensor-core GEMM operands get no
+    launch; the GEMM's operand split reads their source.  Their values then never exist on the device,
+    so verification runs that read back every node lower without it.
+    """
+    folds = foldable_transposes(graph, matmul, keep) if fold else set()
     launches = []
     for node in graph.nodes:
-        if node.op in ("input", "const"):
+        if node.op in ("input", "const") or node.id in folds:
             continue
-        if node.op == "fused":
+        ops = _matmul_operands(graph, node) if folds else None
+        if ops and set(ops) & folds:
+            lau = _folded_launch(graph, node, matmul, sabotage, folds)
+        elif node.op == "fused":
             lau = fused_kernel(node, matmul, sabotage)
         else:
             lau = _plain_launch(graph, node, matmul)
         lau.bytes = _bytes(graph, lau)
         launches.append(lau)
-    return {"launches": launches}
+    return {"launches": launches, "folded": sorted(folds)}

@@ -120,58 +120,87 @@ __device__ __forceinline__ float tf32_rna(float x) {
 #define TCB_SPLITK 1
 #endif
 
-// A [batch, M, K] -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.  It runs first in every
-// tensor-core launch, so it also clears that launch's error word (p[15]) in the reused scratch.
-// Four elements per thread step: 128-bit stores always (Kp % 32 == 0), 128-bit loads when K % 4 == 0.
-extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a) {
-  if (blockIdx.x == 0 && threadIdx.x == 0 && a.p[15]) *reinterpret_cast<u32*>(a.p[15]) = 0u;
-  const float* __restrict__ A = reinterpret_cast<const float*>(a.in[TCB_IA]);
-  float* __restrict__ hi = reinterpret_cast<float*>(a.scratch);
-  float* __restrict__ lo = hi + (u64)TCB_BATCH * TCB_M * TCB_KP;
-  constexpr u64 n4 = (u64)TCB_BATCH * TCB_M * TCB_KP / 4;
+#ifndef TCB_A_T
+#define TCB_A_T 0   // 1: operand A arrives as its transpose X [batch, K, M] (a folded transposeLast2)
+#endif
+#ifndef TCB_B_T
+#define TCB_B_T 0   // 1: operand B arrives as its transpose Y [batch, N, K]
+#endif
+
+namespace tcb {
+// Row-major src [batch, R, C] -> hi, lo [batch, R, Kp] with Kp >= C (zero beyond C), 4 elements per step.
+__device__ __forceinline__ void split_rows(const float* __restrict__ src, float* __restrict__ hi, float* __restrict__ lo,
+                                           u64 rows, u64 C, u64 Kp) {
+  const u64 n4 = rows * Kp / 4;
   for (u64 v = (u64)blockIdx.x * blockDim.x + threadIdx.x; v < n4; v += (u64)gridDim.x * blockDim.x) {
     const u64 i = v * 4;
-    const u64 k = i % TCB_KP, row = i / TCB_KP;
+    const u64 k = i % Kp, row = i / Kp;
     float x[4];
-    if ((TCB_K % 4) == 0 && k + 4 <= (u64)TCB_K) {
-      const float4 q = __ldg(reinterpret_cast<const float4*>(A + row * TCB_K + k));
+    if ((C % 4) == 0 && k + 4 <= C) {
+      const float4 q = __ldg(reinterpret_cast<const float4*>(src + row * C + k));
       x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
     } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] = (k + j < (u64)TCB_K) ? __ldg(A + row * TCB_K + k + j) : 0.0f;
+      for (int j = 0; j < 4; ++j) x[j] = (k + j < C) ? __ldg(src + row * C + k + j) : 0.0f;
     }
     float h[4], l[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) { h[j] = tcb::tf32_rna(x[j]); l[j] = tcb::tf32_rna(x[j] - h[j]); }
+    for (int j = 0; j < 4; ++j) { h[j] = tf32_rna(x[j]); l[j] = tf32_rna(x[j] - h[j]); }
     *reinterpret_cast<float4*>(hi + i) = make_float4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<float4*>(lo + i) = make_float4(l[0], l[1], l[2], l[3]);
   }
 }
-
-// B [batch, K, N] -> B_hi^T, B_lo^T [batch, N, Kp] through 32x32 shared tiles (coalesced both ways).
-extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a) {
+// Row-major src [batch, C, R] -> hi, lo [batch, R, Kp] (transposed), 32x32 tiles through shared memory.
+// grid (Kp/32, ceil(R/32), batch), 256 threads.
+__device__ __forceinline__ void split_cols(const float* __restrict__ src, float* __restrict__ hi, float* __restrict__ lo,
+                                           u64 R, u64 C, u64 Kp) {
   __shared__ float t[32][33];
-  const float* __restrict__ B = reinterpret_cast<const float*>(a.in[TCB_IB]);
-  float* __restrict__ hi = reinterpret_cast<float*>(a.scratch) + 2ull * TCB_BATCH * TCB_M * TCB_KP;
-  float* __restrict__ lo = hi + (u64)TCB_BATCH * TCB_N * TCB_KP;
   const u64 b = blockIdx.z;
-  const u64 k0 = (u64)blockIdx.x * 32, n0 = (u64)blockIdx.y * 32;
+  const u64 k0 = (u64)blockIdx.x * 32, r0 = (u64)blockIdx.y * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int r = ty; r < 32; r += 8) {
-    const u64 k = k0 + r, nn = n0 + tx;
-    t[r][tx] = (k < (u64)TCB_K && nn < (u64)TCB_N) ? __ldg(B + (b * TCB_K + k) * TCB_N + nn) : 0.0f;
+  for (int q = ty; q < 32; q += 8) {
+    const u64 k = k0 + q, r = r0 + tx;
+    t[q][tx] = (k < C && r < R) ? __ldg(src + (b * C + k) * R + r) : 0.0f;
   }
   __syncthreads();
-  for (int r = ty; r < 32; r += 8) {
-    const u64 nn = n0 + r, k = k0 + tx;
-    if (nn < (u64)TCB_N && k < (u64)TCB_KP) {
-      const float x = t[tx][r];
-      const float h = tcb::tf32_rna(x);
-      const u64 o = (b * TCB_N + nn) * TCB_KP + k;
+  for (int q = ty; q < 32; q += 8) {
+    const u64 r = r0 + q, k = k0 + tx;
+    if (r < R && k < Kp) {
+      const float x = t[tx][q];
+      const float h = tf32_rna(x);
+      const u64 o = (b * R + r) * Kp + k;
       hi[o] = h;
-      lo[o] = tcb::tf32_rna(x - h);
+      lo[o] = tf32_rna(x - h);
     }
   }
+}
+}  // namespace tcb
+
+// A -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.  It runs first in every tensor-core
+// launch, so it also clears that launch's error word (p[15]) in the reused scratch.
+extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a) {
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0 && a.p[15])
+    *reinterpret_cast<u32*>(a.p[15]) = 0u;
+  float* hi = reinterpret_cast<float*>(a.scratch);
+  float* lo = hi + (u64)TCB_BATCH * TCB_M * TCB_KP;
+  const float* src = reinterpret_cast<const float*>(a.in[TCB_IA]);
+#if TCB_A_T
+  tcb::split_cols(src, hi, lo, TCB_M, TCB_K, TCB_KP);
+#else
+  tcb::split_rows(src, hi, lo, (u64)TCB_BATCH * TCB_M, TCB_K, TCB_KP);
+#endif
+}
+
+// B [batch, K, N] -> B_hi^T, B_lo^T [batch, N, Kp] so both operands are K-major.
+extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a) {
+  float* hi = reinterpret_cast<float*>(a.scratch) + 2ull * TCB_BATCH * TCB_M * TCB_KP;
+  float* lo = hi + (u64)TCB_BATCH * TCB_N * TCB_KP;
+  const float* src = reinterpret_cast<const float*>(a.in[TCB_IB]);
+#if TCB_B_T
+  tcb::split_rows(src, hi, lo, (u64)TCB_BATCH * TCB_N, TCB_K, TCB_KP);
+#else
+  tcb::split_cols(src, hi, lo, TCB_N, TCB_K, TCB_KP);
+#endif
 }
 
 extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_constant__ tcb::GemmParams P) {

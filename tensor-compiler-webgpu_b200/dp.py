@@ -90,7 +90,7 @@ class DPTrainer:
         # a gradient the graph gives as a constant zero (no dependence) is still written by its launch
         for gid, off in zip(grad_ids, offs):
             place_g[gid] = self.flat.ptr + off
-        lowered_g = lower_fused(fg.graph, matmul=matmul)
+        lowered_g = lower_fused(fg.graph, matmul=matmul, fold=True, keep=[self.loss_id, *grad_ids])
         self.grad_prog = rt.Program(runner, fg.graph, lowered_g, keep=[self.loss_id], place=place_g)
         fa = fuse(ad["graph"], keep=list(ad["outputs"].values()))
         place_a = {}

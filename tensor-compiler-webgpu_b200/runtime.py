@@ -451,30 +451,53 @@ class Program:
     feedback, src/gpu/trainer.js:64).
     """
 
-    def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False, place=None):
-        """`place` maps node ids to device addresses owned by the caller (e.g. slices of one flat buffer)."""
+    def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False, place=None, alias=True):
+        """`place` maps node ids to device addresses owned by the caller (e.g. slices of one flat buffer).
+
+        `alias`: a plain reshape launch is dropped and its value shares its source's memory (a row-major
+        reshape moves no bytes); lifetimes are merged along alias chains.
+        """
         self.runner = runner
         self.graph = graph
-        self.launches = lowered["launches"]
         nodes = graph.nodes
         self.own = {}
         keep = set(keep)
-        first = {}
-        last = {}
+        place = place or {}
+        fb = {i for pair in feedback for i in pair}
+        self.alias = {}
+        launches = []
+        for lau in lowered["launches"]:
+            n = nodes[lau.node]
+            if (alias and n.op == "reshape" and lau.kind == "gather" and lau.node not in keep
+                    and lau.node not in place and lau.node not in fb):
+                self.alias[lau.node] = lau.inputs[0]
+                continue
+            launches.append(lau)
+        self.launches = launches
+
+        def root(i):
+            while i in self.alias:
+                i = self.alias[i]
+            return i
+        first, last = {}, {}
         for k, lau in enumerate(self.launches):
             first[lau.node] = k
             for i in lau.inputs:
-                last[i] = k
+                r = root(i)
+                last[r] = max(last.get(r, -1), k)
+        consumed = set(last)
         arena_ids = []
-        place = place or {}
         for node in nodes:
             nbytes = max(1, size(node.shape)) * 4
-            if node.id in place:
+            if node.id in place or node.id in self.alias:
                 continue
-            if node.op in ("input", "const") or node.id in keep or node.id not in first:
+            if node.op in ("input", "const") or node.id in keep or node.id in fb:
                 self.own[node.id] = DeviceBuffer(runner, nbytes)
-            else:
+            elif node.id in first:
                 arena_ids.append(node.id)
+            elif node.id in consumed:
+                self.own[node.id] = DeviceBuffer(runner, nbytes)
+            # else: never produced nor read (a folded transpose): no memory
         offs, total = plan_memory([max(1, size(nodes[i].shape)) * 4 for i in arena_ids],
                                   [first[i] for i in arena_ids], [last.get(i, first[i]) for i in arena_ids])
         self.arena_bytes = total
@@ -483,6 +506,8 @@ class Program:
         self.ptrs.update(place)
         for i, o in zip(arena_ids, offs):
             self.ptrs[i] = self.arena.ptr + o
+        for a in self.alias:
+            self.ptrs[a] = self.ptrs[root(a)]
         for node in nodes:
             if node.op == "const" and node.id in self.own:
                 v = node.attrs["value"]

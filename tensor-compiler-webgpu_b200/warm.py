@@ -50,7 +50,8 @@ def standard_sources(full=True):
         cfg, c = wl.c5_cfg()
         gs = _steps.build_grad3b(c["V"], c["batch"], cfg)
         f = fuse(gs["graph"], keep=[gs["loss"], *gs["grads"].values()])
-        codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul="tiled")["launches"]}
+        keep = [f.index[i] for i in [gs["loss"], *gs["grads"].values()]]
+        codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=keep)["launches"]}
         ad = _steps.build_adam_graph(c["V"], cfg)
         fa = fuse(ad["graph"], keep=list(ad["outputs"].values()))
         codes |= {lau.code for lau in cg.lower_fused(fa.graph, matmul="tiled")["launches"]}

@@ -83,3 +83,21 @@ def test_fused_launches_replace_the_plain_ones(pkg, cg):
     plain = cg.lower(W["graph"])["launches"]
     assert len(fused) < len(plain)
     assert sum(1 for l in fused if l.kind == "fused-elementwise") == 4
+
+
+def test_transpose_folding_picks_only_gemm_operand_transposes(pkg, cg):
+    g = pkg.ir.Graph()
+    a = g.input("a", [64, 96])
+    w = g.input("w", [48, 64])
+    t = g.transpose(w, [1, 0])            # read only as a GEMM operand: folded
+    y = g.matmul(a, g.transpose(t, [1, 0]) if False else g.transpose(w, [1, 0]))
+    u = g.transpose(a, [1, 0])            # also read by an elementwise op: kept
+    z = g.add(g.matmul(u, a), g.const(1.0))
+    v = g.exp(u)
+    folds = cg.foldable_transposes(g, "tiled")
+    low = cg.lower(g, matmul="tiled", fold=True)
+    assert u not in folds
+    assert all(g.nodes[i].op == "transpose" for i in folds) and folds
+    mm = [l for l in low["launches"] if l.op == "matmul"]
+    assert any(l.info.get("b_t") for l in mm)
+    assert cg.foldable_transposes(g, "naive") == set()   # CUDA-core path: nothing folds

@@ -70,3 +70,35 @@ def test_dp_trainer_world1_matches_fused_step(pkg, runner):
     finally:
         ref.destroy()
         tr.destroy()
+
+
+def test_folded_transposes_and_aliased_reshapes_change_no_bit(pkg, runner):
+    """The resident program (transposes folded into GEMM operand splits, reshapes aliased) gives the
+    verification path's values bit for bit on the loss and every gradient."""
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    cg = importlib.import_module("tensor-compiler-webgpu_b200.codegen")
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    s = pkg.steps
+    cfg, c = wl.c5_cfg(d=64, L=2, H=4, ff=128, T=32, batch=4)
+    V, B = c["V"], c["batch"]
+    gs = s.build_grad3b(V, B, cfg)
+    f = pkg.fuse.fuse(gs["graph"], keep=[gs["loss"], *gs["grads"].values()])
+    keep = [f.index[i] for i in [gs["loss"], *gs["grads"].values()]]
+    params = s.init_params_normal(V, 0, 0.02, cfg)
+    x, y = wl.one_hot_batch(wl.c5_tokens(B, cfg["T"], V), V)
+    feed = {**params, "x": x, "y": y, gs["cotangent"]: [1.0]}
+    plain = runner.run(f.graph, cg.lower_fused(f.graph, matmul="tiled"),
+                       {n.attrs["name"]: feed[n.attrs["name"]] for n in f.graph.inputs()})
+    low = cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=keep)
+    assert low["folded"], "the C5 backward has transposes feeding GEMMs"
+    prog = rt.Program(runner, f.graph, low, keep=keep)
+    try:
+        assert prog.alias, "the C5 graph has plain reshapes to alias"
+        for n in f.graph.inputs():
+            prog.write(n.id, feed[n.attrs["name"]])
+        prog.run()
+        prog.check_errors()
+        for k in keep:
+            assert np.array_equal(prog.read(k).view(np.uint32), plain["values"][k].view(np.uint32)), k
+    finally:
+        prog.free()
