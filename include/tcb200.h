@@ -93,6 +93,9 @@ int tc_compile(tc_ctx* ctx, const char* cuda_src, tc_module** out, char* log, si
 int tc_compile_check(const char* cuda_src, char* log, size_t log_cap, uint64_t* cubin_bytes);
 /* Compile to a cubin image in caller memory (no device needed); with out == NULL only the size is returned. */
 int tc_compile_cubin(const char* cuda_src, void* out, uint64_t cap, uint64_t* cubin_bytes, char* log, size_t log_cap);
+/* A hash of the sm_100a templates compiled into this library: part of any on-disk kernel cache key, so
+ * a cubin built against other template text is never reused. */
+uint64_t tc_templates_hash(void);
 /* Load a cubin made by tc_compile_cubin (e.g. from an on-disk kernel cache). */
 int tc_module_load(tc_ctx* ctx, const void* cubin, uint64_t bytes, tc_module** out);
 int tc_module_free(tc_module* mod);

@@ -101,6 +101,17 @@ static int bind(tc_ctx* ctx) {
 extern "C" {
 
 const char* tc_last_error(void) { return g_err.c_str(); }
+
+uint64_t tc_templates_hash(void) {
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < sizeof(kTemplates) / sizeof(kTemplates[0]); i++) {
+    h ^= fnv1a(kTemplates[i].name, strlen(kTemplates[i].name));
+    h *= 1099511628211ull;
+    h ^= fnv1a(kTemplates[i].text, strlen(kTemplates[i].text));
+    h *= 1099511628211ull;
+  }
+  return h;
+}
 int tc_version(void) { return 1; }
 
 int tc_open(int device_ordinal, tc_ctx** out) {

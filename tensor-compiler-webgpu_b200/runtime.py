@@ -49,6 +49,7 @@ _lib = None
 _SIGS = {
     "tc_last_error": ([], ctypes.c_char_p),
     "tc_version": ([], ctypes.c_int),
+    "tc_templates_hash": ([], ctypes.c_uint64),
     "tc_open": ([ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "tc_close": ([ctypes.c_void_p], ctypes.c_int),
     "tc_info": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
@@ -153,8 +154,10 @@ CACHE_DIR = os.environ.get("TCB_KERNEL_CACHE", os.path.join(os.path.dirname(os.p
 
 
 def _cache_path(code):
+    """Cache file of a kernel: keyed by its source AND the library's embedded template text."""
     import hashlib
-    return os.path.join(CACHE_DIR, hashlib.sha256(code.encode()).hexdigest()[:32] + ".cubin")
+    key = hashlib.sha256(code.encode() + b"\0" + str(lib().tc_templates_hash()).encode()).hexdigest()[:32]
+    return os.path.join(CACHE_DIR, key + ".cubin")
 
 
 def compile_cubin(code):
@@ -209,13 +212,17 @@ def _map_desc(call, scratch):
     return (ctypes.c_uint64 * len(vals))(*vals)
 
 
-def issue(call, mod, ins, out, scratch, plan=None, ctx=None):
-    """Launch one KernelCall now (plan None) or append it to a native plan."""
+def issue(call, mod, ins, out, scratch, plan=None, err_ptr=None):
+    """Launch one KernelCall now (plan None) or append it to a native plan.
+
+    A call with an error word gets its address in p[15]: `err_ptr` when given (a resident program's own
+    word for that launch), else its slot in the scratch buffer.
+    """
     params = list(call.params)
     if call.err_offset is not None:
         while len(params) < 16:
             params.append(0)
-        params[15] = scratch + call.err_offset
+        params[15] = err_ptr if err_ptr is not None else scratch + call.err_offset
     args = make_args(ins, out, scratch, params)
     g, b = _u32x3(call.grid), _u32x3(call.block)
     if call.tma:
@@ -518,15 +525,23 @@ class Program:
         self.scratch = DeviceBuffer(runner, scratch_bytes) if scratch_bytes else None
         if self.scratch:
             check(lib().tc_memset32(runner.ctx, self.scratch.ptr, 0, scratch_bytes // 4))
+        # one error word per launch that has one (launches share scratch, so not there)
+        self.err_slot = {}
+        for k, lau in enumerate(self.launches):
+            if any(c.err_offset is not None for c in lau.calls):
+                self.err_slot[k] = len(self.err_slot)
+        self.errs = DeviceBuffer(runner, 4 * max(1, len(self.err_slot)))
+        check(lib().tc_memset32(runner.ctx, self.errs.ptr, 0, max(1, len(self.err_slot))))
         h = ctypes.c_void_p()
         check(lib().tc_plan_create(runner.ctx, ctypes.byref(h)))
         self.plan = h
         self.kernel_launches = 0
-        for lau in self.launches:
+        for k, lau in enumerate(self.launches):
             mod = runner.pipeline(lau.code)
             ins = [self.ptrs[i] for i in lau.inputs]
             for call in lau.calls:
-                issue(call, mod, ins, self.ptrs[lau.node], self.scratch.ptr if self.scratch else 0, plan=h)
+                issue(call, mod, ins, self.ptrs[lau.node], self.scratch.ptr if self.scratch else 0, plan=h,
+                      err_ptr=self.err_ptr(k))
                 self.kernel_launches += 1
         for src, dst in feedback:
             check(lib().tc_plan_add_copy(h, self.ptrs[dst], self.ptrs[src], max(1, size(nodes[dst].shape)) * 4))
@@ -564,11 +579,20 @@ class Program:
     def run(self):
         check(lib().tc_plan_run(self.plan))
 
+    def err_ptr(self, k):
+        return self.errs.ptr + 4 * self.err_slot[k] if k in self.err_slot else None
+
     def check_errors(self):
-        """Raise if any tensor-core launch's bounded wait ran out (reads the error words after a sync)."""
-        if self.scratch:
-            for lau in self.launches:
-                self.runner.check_errors(lau, self.scratch.ptr)
+        """Raise if any tensor-core launch's bounded wait ran out (its own error word, read after a sync)."""
+        if not self.err_slot:
+            return
+        self.runner.sync()
+        w = self.errs.download(len(self.err_slot), np.uint32)
+        bad = [k for k, slot in self.err_slot.items() if w[slot]]
+        if bad:
+            check(lib().tc_memset32(self.runner.ctx, self.errs.ptr, 0, len(self.err_slot)))
+            raise TcError(5, f"launch {bad[0]} ({self.launches[bad[0]].kind}): a bounded wait ran out "
+                             f"(code {int(w[self.err_slot[bad[0]]])})")
 
     def free(self):
         if self.plan:
@@ -583,6 +607,9 @@ class Program:
         if self.scratch:
             self.scratch.free()
             self.scratch = None
+        if getattr(self, "errs", None):
+            self.errs.free()
+            self.errs = None
 
 
 def fused_step(step, sabotage=None, pass_sabotage=None, matmul="naive"):
@@ -662,15 +689,16 @@ class Segments:
     def __init__(self, prog, cuts):
         self.prog = prog
         self.plans = []
-        flat = [(lau, call) for lau in prog.launches for call in lau.calls]
+        flat = [(k, lau, call) for k, lau in enumerate(prog.launches) for call in lau.calls]
         bounds = [0, *cuts, len(flat)]
         scratch = prog.scratch.ptr if prog.scratch else 0
         for a, b in zip(bounds[:-1], bounds[1:]):
             h = ctypes.c_void_p()
             check(lib().tc_plan_create(prog.runner.ctx, ctypes.byref(h)))
-            for lau, call in flat[a:b]:
+            for k, lau, call in flat[a:b]:
                 mod = prog.runner.pipeline(lau.code)
-                issue(call, mod, [prog.ptrs[i] for i in lau.inputs], prog.ptrs[lau.node], scratch, plan=h)
+                issue(call, mod, [prog.ptrs[i] for i in lau.inputs], prog.ptrs[lau.node], scratch, plan=h,
+                      err_ptr=prog.err_ptr(k))
             self.plans.append(h)
 
     def run(self, k):
