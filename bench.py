@@ -24,6 +24,8 @@ import subprocess
 import sys
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 PKG = "tensor-compiler-webgpu_b200"
@@ -145,7 +147,23 @@ def build_workload(name, wl, pkg, cg, rows=None):
 
 
 def cpu_sample(name, wl, pkg, cg, rows):
-    """The same workload cut to `rows` rows (rows are independent in C2 and C4): graph, inputs, bytes."""
+    """The same workload cut to `rows` rows (rows are independent in C2 and C4): graph, inputs, units.
+
+    Units are the metric's: algorithmic bytes (C2, C4), useful flops (C3), samples (C1), tokens (C5:
+    `rows` sequences of the full training step: forward, backward and Adam).
+    """
+    if name == "c1":
+        step = wl.c1_step(64)
+        inputs = wl.c1_inputs(64)
+        inputs[step["cotangent"]] = [1.0]
+        return step["graph"], inputs, 64
+    if name == "c5":
+        cfg, c = wl.c5_cfg()
+        st = pkg.steps.build_step3b(c["V"], rows, cfg)
+        params = pkg.steps.init_params_normal(c["V"], 0, 0.02, cfg)
+        state = pkg.steps.adam_initial_state(st["names"], pkg.steps.param_shapes(c["V"], cfg))
+        x, y = wl.one_hot_batch(wl.c5_tokens(rows, cfg["T"], c["V"]), c["V"])
+        return st["graph"], {**params, **state, "x": x, "y": y, st["cotangent"]: [1.0]}, rows * cfg["T"]
     if name == "c2":
         W = wl.c2_graph(rows, 8192)
         inputs = wl.c2_inputs(W)
@@ -155,6 +173,8 @@ def cpu_sample(name, wl, pkg, cg, rows):
     else:
         W = wl.c3_graph(rows, 4096, 4096, "relu")
         inputs = wl.c3_inputs(rows, 4096, 4096)
+    if name == "c3":
+        return W["graph"], inputs, 2 * rows * 4096 * 4096
     fused = pkg.fuse.fuse(W["graph"], keep=W["keep"])
     nbytes = sum(l.bytes for l in cg.lower_fused(fused.graph)["launches"])
     return W["graph"], inputs, nbytes
@@ -363,7 +383,7 @@ def cpu_baseline(name, pkg, cg, wl, seconds):
             break
         rows = min(full, max(rows * 2, int(rows * seconds / max(dt, 1e-3) / 1.5)))
     if name == "c3":
-        return {"value": round(2 * rows * 4096 * 4096 / dt / 1e12, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
+        return {"value": round(nbytes / dt / 1e12, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
                 "sample": f"{rows} of 4096 rows of A (the interpreter is linear in M), triple loop once in {dt:.2f} s "
                           f"(C restatement of interp.js, float64, single thread, gcc -O2)", "seconds": round(dt, 3)}
     return {"value": round(nbytes / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
@@ -381,7 +401,7 @@ def run_reference(args):
     pkg, _, cg, wl = (importlib.import_module(PKG), None, importlib.import_module(PKG + ".codegen"),
                       importlib.import_module(PKG + ".workloads"))
     cores = os.cpu_count() or 1
-    rows = {"c2": 64, "c4": 16, "c3": 1}[args.workload]
+    rows = {"c2": 64, "c4": 16, "c3": 1, "c1": 1, "c5": 1}[args.workload]
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
         # every worker prepares its sample once (untimed); a step is every worker evaluating it once
@@ -394,20 +414,25 @@ def run_reference(args):
                 times.append(max(t for _, t in res))
                 total_bytes += sum(b for b, _ in res)
     wall = sum(times)
-    value = total_bytes / wall / 1e9
-    full = {"c2": 8192, "c4": 65536, "c3": 4096}[args.workload]
-    sample = (f"{cores} processes x {rows} of {full} rows per step, step time = slowest process "
-              f"(C restatement of interp.js, float64)")
-    out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+    unit, scale = {"c1": ("samples/s", 1), "c5": ("tokens/s", 1), "c3": ("TFLOP/s", 1e-12)}.get(
+        args.workload, ("GB/s", 1e-9))
+    value = total_bytes / wall * scale
+    what = {"c1": "the whole C1 step graph", "c5": "1 sequence of the C5 training step (forward, backward, Adam)"}
+    full = {"c2": 8192, "c4": 65536, "c3": 4096}.get(args.workload)
+    sample = (f"{cores} processes x " + (what[args.workload] if args.workload in what else f"{rows} of {full} rows") +
+              " per step, step time = slowest process (C restatement of interp.js, float64)")
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": unit, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * wall / len(times), 2),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
            "data": "synthetic (mulberry32 seed 0)",
            "config": {"workload": {"c2": "C2 elementwise chain fp32 [8192,8192] fwd+bwd",
                                    "c4": "C4 softmax fp32 [65536,4096] fwd+bwd, 1% rows +800",
-                                   "c3": "C3 matmul 4096^3 + bias + relu (fp32)"}[args.workload]},
-           "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                                   "c3": "C3 matmul 4096^3 + bias + relu (fp32)",
+                                   "c1": "C1 MLP 64->32->10 tanh, batch 64, fwd+bwd",
+                                   "c5": "C5 decoder transformer train step (fwd+bwd+Adam)"}[args.workload]},
+           "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": cores, "kind": "port",
                             "sample": sample},
-           "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+           "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
 
@@ -416,7 +441,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c3", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c4", "c3", "c5"])
     ap.add_argument("--batch", type=int, default=None, help="C5 global batch (default 512)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
@@ -430,6 +455,8 @@ def main():
         run_reference(args)
     elif args.workload == "c5":
         run_c5(args)
+    elif args.workload == "c1":
+        run_c1(args)
     else:
         run_ours(args)
 
@@ -535,6 +562,93 @@ def run_c5(args):
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_c1(args):
+    """C1: the MLP 64 -> 32 -> 10 (tanh) step, batch 64, forward + backward fused; samples/s (launch-bound)."""
+    world, rank, local = _dist()
+    pkg, rt, cg, wl = _mods()
+    step = wl.c1_step(64)
+    inputs = wl.c1_inputs(64)
+    inputs[step["cotangent"]] = [1.0]
+    keep = [step["loss"], *step["outputs"].values()]
+    fused = pkg.fuse.fuse(step["graph"], keep=keep)
+    lowered = cg.lower_fused(fused.graph, matmul="naive")
+    outs = [fused.index[k] for k in keep]
+    runner = rt.GpuRunner.create(local)
+    prog = rt.Program(runner, fused.graph, lowered, keep=outs)
+    name_of = {n.id: n.attrs["name"] for n in fused.graph.nodes if n.op == "input"}
+    for nid, name in name_of.items():
+        prog.write(nid, inputs[name])
+    prog.capture()
+    K, Wm = max(args.steps, 100), args.warmup
+    for _ in range(Wm):
+        prog.run()
+    runner.sync()
+    ev = rt.Events(runner, 2)
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev.record(0)
+    for _ in range(K):
+        prog.run()
+    ev.record(1)
+    runner.sync()
+    clk = clocks.stop()
+    us = ev.ms(0, 1) / K * 1e3
+    # end to end: x, y from pinned host memory, the step, the loss and the gradients back
+    xin = [nid for nid, nm in name_of.items() if nm in ("x", "y")]
+    hosts = {nid: rt.PinnedHost(np.asarray(inputs[name_of[nid]], np.float32).nbytes) for nid in xin}
+    for nid in xin:
+        hosts[nid].array(hosts[nid].nbytes // 4)[:] = np.asarray(inputs[name_of[nid]], np.float32).reshape(-1)
+    osz = {o: pkg.ir.size(fused.graph.nodes[o].shape) for o in outs}
+    hout = {o: rt.PinnedHost(osz[o] * 4) for o in outs}
+    lib = rt.lib()
+
+    def e2e():
+        for nid in xin:
+            prog.write_async(nid, hosts[nid].ptr, hosts[nid].nbytes)
+        prog.run()
+        for o in outs:
+            rt.check(lib.tc_memcpy_dtoh(runner.ctx, hout[o].ptr, prog.ptr(o), osz[o] * 4))
+    e2e()
+    runner.sync()
+    ev.record(0)
+    for _ in range(K):
+        e2e()
+    ev.record(1)
+    runner.sync()
+    e2e_us = ev.ms(0, 1) / K * 1e3
+    result = {"metric": METRIC, "value": round(64 / (us / 1e6), 1), "unit": "samples/s", "n_gpus": world,
+              "steps": K, "warmup": Wm, "ms_per_step": round(us / 1e3, 5), "higher_is_better": True, "scaling": "weak",
+              "vs_baseline": None, "dtype": "f32", "data": "synthetic (features int(0..16)/16, labels 0..9, Glorot weights)",
+              "config": {"workload": "C1 MLP 64->32->10 tanh, batch 64, fwd+bwd (fused, one CUDA graph)",
+                         "launches_per_step": prog.kernel_launches, "us_per_step": round(us, 2)},
+              "roofline": {"bound": "launch", "achieved": round(us / prog.kernel_launches, 3), "peak": None,
+                           "unit": "us per kernel", "frac": None, "traffic": None,
+                           "kernel": "whole step (launch-latency bound: tens of tiny kernels)"},
+              "e2e": {"value": round(64 / (e2e_us / 1e6), 1), "unit": "samples/s",
+                      "h2d_bytes_per_step": sum(h.nbytes for h in hosts.values()),
+                      "d2h_bytes_per_step": sum(osz[o] * 4 for o in outs), "us_per_step": round(e2e_us, 2)},
+              "gpu_launches": K * prog.kernel_launches, "clocks": clk}
+    if rank == 0 and not args.no_cpu:
+        oracle = _oracle()
+        graph = step["graph"]
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 5.0):
+            oracle.evaluate(graph, inputs, want=[])
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        result["cpu_baseline"] = {"value": round(64 / dt, 1), "unit": "samples/s", "cores": 1, "kind": "port",
+                                  "sample": f"the whole step graph, {reps} evaluations (C restatement of interp.js)"}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    for h in list(hosts.values()) + list(hout.values()):
+        h.free()
+    ev.free()
+    prog.free()
+    runner.close()
 
 
 def _matmul_flops(pkg, graph):
