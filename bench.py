@@ -436,6 +436,36 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_sweep(args):
+    """The amendment-34 sweep and the copy/read ceilings under amendment 32's protocol (not the driver's line)."""
+    tm = importlib.import_module(PKG + ".timing")
+    rt = importlib.import_module(PKG + ".runtime")
+    codes = set()
+    for w in tm.workloads():
+        if args.only and not any(x in w["id"] for x in args.only.split(",")):
+            continue
+        for prog in tm.build_variants(w)["programs"].values():
+            codes |= {d["code"] for d in prog["dispatches"]}
+    codes |= {c["program"]["dispatches"][0]["code"] for c in tm.ceiling_programs()}
+    rt.precompile(codes)
+    bench = tm.Bench.create(0)
+    out = open(args.sweep, "w")
+
+    def log(rec):
+        out.write(json.dumps(rec) + "\n")
+        out.flush()
+        if rec["family"] == "ceiling":
+            print(f"{rec['id']:32s} {rec['GBps']:9.1f} GB/s", flush=True)
+        else:
+            v = "  ".join(f"{k} {d['GBps']:8.1f} GB/s ({d['launches']})" for k, d in rec["variants"].items())
+            print(f"{rec['id']:36s} {v}", flush=True)
+    res = tm.run_sweep(bench, only=args.only.split(",") if args.only else None, log=log)
+    out.close()
+    bench.close()
+    leaks = [r["id"] for r in res if r["created"]]
+    print(json.dumps({"sweep": len(res), "objects_created_in_timed_regions": leaks}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -448,10 +478,14 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--rows", type=int, default=None, help="cut C2/C4 to fewer rows (profiling cases only)")
+    ap.add_argument("--sweep", default=None, help="run the amendment-34 sweep, one JSON record per line to this file")
+    ap.add_argument("--only", default=None, help="sweep: comma-separated id substrings")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "c5":
         run_c5(args)

@@ -58,5 +58,17 @@ def standard_sources(full=True):
     return codes
 
 
+def sweep_sources():
+    from . import timing as tm
+    codes = set()
+    for w in tm.workloads():
+        for p in tm.build_variants(w)["programs"].values():
+            codes |= {d["code"] for d in p["dispatches"]}
+    return codes | {c["program"]["dispatches"][0]["code"] for c in tm.ceiling_programs()}
+
+
 def warm(full=True):
-    return rt.precompile(standard_sources(full))
+    codes = standard_sources(full)
+    if full:
+        codes |= sweep_sources()
+    return rt.precompile(codes)
