@@ -39,6 +39,11 @@ def main(ref):
     pins = {"source": "golden/measurements.json m4; golden/spec-m3b.json golden[0]",
             "fusion": m["fusion"], "semanticsModel": m["semantics"]["model"],
             "corpusByPattern": m["semantics"]["corpus"]["byPattern"],
+            "corpus": {k: m["semantics"]["corpus"][k] for k in ("programs", "graphs", "withFused", "identical",
+                                                                "compared", "fusedNodes", "byPattern")},
+            "gpuFuzz": {k: m["gpu"]["fuzz"][k] for k in ("programs", "skipped", "runs", "fusedRuns", "unfusedPassed",
+                                                         "fusedPassed", "bitwiseSame")}
+            if "fuzz" in m.get("gpu", {}) else None,
             "goldenConfig": {k: g0[k] for k in ("name", "seed", "V", "batch")},
             "gpuLaunches": m["gpu"].get("teacherForced", {}).get("launches")}
     json.dump(pins, open(os.path.join(HERE, "pins.json"), "w"), indent=1)
