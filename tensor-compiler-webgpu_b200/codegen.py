@@ -328,12 +328,17 @@ class _RowLoads:
     def leaf(self, k, ctx):
         T = self.T
         ptr = f"reinterpret_cast<const float*>(a.in[{k}])"
-        if ctx.key == "r":
-            key = ("r", k)
+        root = ctx
+        while root.parent is not None:
+            root = root.parent
+        if root.key == "r":
+            # a row-context read (possibly through a broadcast of the operand): once per row
+            key = (ctx.key, k)
             if key not in self.row:
                 name = f"R{len(self.row)}"
                 self.row[key] = name
-                self.order_row.append(f"const float {name} = active ? tcb::ld1({ptr} + ({T})r) : 0.0f;")
+                idx = _chain_index(ctx, f"({T})r", T)
+                self.order_row.append(f"const float {name} = active ? tcb::ld1({ptr} + {idx}) : 0.0f;")
             return self.row[key]
         # element context (or a gathered child of it)
         g = ctx.gather

@@ -67,8 +67,25 @@ def sweep_sources():
     return codes | {c["program"]["dispatches"][0]["code"] for c in tm.ceiling_programs()}
 
 
+def fuzz_sources(every=10):
+    """Kernels of the differential fuzzer's runs over corpus programs i % every in {1, 2}."""
+    from .autodiff import grad
+    from .corpus import corpus_program
+    codes = set()
+    for i in range(1, 2001):
+        if every != 1 and i % every not in (1, 2):
+            continue
+        p = corpus_program(i, f32=True)
+        G = grad(p.graph, p.outputs, [n.id for n in p.graph.inputs()])
+        mms = ("naive", "tiled") if any(n.op == "matmul" for n in p.graph.nodes) else ("naive",)
+        for mm in mms:
+            for g, keep in ((p.graph, p.outputs), (G.graph, list(p.outputs) + list(G.grads))):
+                codes |= _codes(g, keep, mm)
+    return codes
+
+
 def warm(full=True):
     codes = standard_sources(full)
     if full:
-        codes |= sweep_sources()
+        codes |= sweep_sources() | fuzz_sources(10)
     return rt.precompile(codes)
