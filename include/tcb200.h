@@ -112,6 +112,15 @@ int tc_launch_tma(tc_module* mod, const char* kernel, const uint32_t grid[3], co
                   uint32_t smem_bytes, int n_maps, const uint64_t* map_desc /* 8 per map */,
                   const tc_args* args);
 
+/* ---- extra streams (pipelining copies against compute): handles are CUstreams ---- */
+int tc_stream_create(tc_ctx* ctx, uint64_t* stream);
+int tc_stream_destroy(tc_ctx* ctx, uint64_t stream);
+int tc_memcpy_htod_on(tc_ctx* ctx, uint64_t dst, const void* host, uint64_t bytes, uint64_t stream);
+int tc_memcpy_dtoh_on(tc_ctx* ctx, void* host, uint64_t src, uint64_t bytes, uint64_t stream);
+int tc_event_record_on(tc_ctx* ctx, uint64_t ev, uint64_t stream);
+int tc_stream_wait_event(tc_ctx* ctx, uint64_t stream, uint64_t ev);
+int tc_event_sync(uint64_t ev, int timeout_ms);    /* bounded wait for an event; TC_ERR_TIMEOUT when it runs out */
+
 /* ---- synchronisation and timing ---- */
 int tc_sync(tc_ctx* ctx, int timeout_ms);          /* TC_ERR_TIMEOUT when the wait runs out */
 int tc_event_create(tc_ctx* ctx, uint64_t* ev);
@@ -131,6 +140,7 @@ int tc_plan_add_launch_tma(tc_plan* plan, tc_module* mod, const char* kernel, co
                            const tc_args* args);
 int tc_plan_add_copy(tc_plan* plan, uint64_t dst, uint64_t src, uint64_t bytes);
 int tc_plan_run(tc_plan* plan);                    /* every entry, in order, on the context's stream */
+int tc_plan_run_on(tc_plan* plan, uint64_t stream);  /* the same on another stream of the context */
 int tc_plan_capture(tc_plan* plan);                /* later runs replay one CUDA graph */
 int tc_plan_launch_count(tc_plan* plan, int* n);
 int tc_plan_free(tc_plan* plan);

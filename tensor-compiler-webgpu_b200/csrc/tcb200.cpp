@@ -540,6 +540,57 @@ int tc_sync(tc_ctx* ctx, int timeout_ms) {
   return TC_OK;
 }
 
+int tc_stream_create(tc_ctx* ctx, uint64_t* stream) {
+  if (!stream) return fail(TC_ERR_INVALID, "null out");
+  if (int s = bind(ctx)) return s;
+  CUstream st;
+  CU_TRY(CU(cuStreamCreate)(&st, CU_STREAM_NON_BLOCKING));
+  *stream = (uint64_t)(uintptr_t)st;
+  return TC_OK;
+}
+
+int tc_stream_destroy(tc_ctx* ctx, uint64_t stream) {
+  if (int s = bind(ctx)) return s;
+  if (stream) CU_TRY(CU(cuStreamDestroy)((CUstream)(uintptr_t)stream));
+  return TC_OK;
+}
+
+int tc_memcpy_htod_on(tc_ctx* ctx, uint64_t dst, const void* host, uint64_t bytes, uint64_t stream) {
+  if (int s = bind(ctx)) return s;
+  if (bytes) CU_TRY(CU(cuMemcpyHtoDAsync)((CUdeviceptr)dst, host, bytes, (CUstream)(uintptr_t)stream));
+  return TC_OK;
+}
+
+int tc_memcpy_dtoh_on(tc_ctx* ctx, void* host, uint64_t src, uint64_t bytes, uint64_t stream) {
+  if (int s = bind(ctx)) return s;
+  if (bytes) CU_TRY(CU(cuMemcpyDtoHAsync)(host, (CUdeviceptr)src, bytes, (CUstream)(uintptr_t)stream));
+  return TC_OK;
+}
+
+int tc_event_record_on(tc_ctx* ctx, uint64_t ev, uint64_t stream) {
+  if (int s = bind(ctx)) return s;
+  CU_TRY(CU(cuEventRecord)((CUevent)(uintptr_t)ev, (CUstream)(uintptr_t)stream));
+  return TC_OK;
+}
+
+int tc_stream_wait_event(tc_ctx* ctx, uint64_t stream, uint64_t ev) {
+  if (int s = bind(ctx)) return s;
+  CU_TRY(CU(cuStreamWaitEvent)((CUstream)(uintptr_t)stream, (CUevent)(uintptr_t)ev, 0));
+  return TC_OK;
+}
+
+int tc_event_sync(uint64_t ev, int timeout_ms) {
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    CUresult r = CU(cuEventQuery)((CUevent)(uintptr_t)ev);
+    if (r == CUDA_SUCCESS) return TC_OK;
+    if (r != CUDA_ERROR_NOT_READY) return fail(TC_ERR_CUDA, "event: %s", cu_name(r));
+    double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (timeout_ms >= 0 && ms > timeout_ms) return fail(TC_ERR_TIMEOUT, "event not reached after %d ms", timeout_ms);
+    std::this_thread::sleep_for(std::chrono::microseconds(ms < 5 ? 10 : 200));
+  }
+}
+
 int tc_event_create(tc_ctx* ctx, uint64_t* ev) {
   if (!ev) return fail(TC_ERR_INVALID, "null out");
   if (int s = bind(ctx)) return s;
@@ -667,6 +718,15 @@ int tc_plan_run(tc_plan* plan) {
     return TC_OK;
   }
   return plan_issue(plan);
+}
+
+int tc_plan_run_on(tc_plan* plan, uint64_t stream) {
+  if (!plan) return fail(TC_ERR_INVALID, "null plan");
+  CUstream saved = plan->ctx->stream;
+  plan->ctx->stream = stream ? (CUstream)(uintptr_t)stream : plan->ctx->own_stream;
+  int s = tc_plan_run(plan);
+  plan->ctx->stream = saved;
+  return s;
 }
 
 int tc_plan_capture(tc_plan* plan) {

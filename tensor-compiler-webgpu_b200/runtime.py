@@ -82,6 +82,16 @@ _SIGS = {
                        ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint32, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64),
                        ctypes.POINTER(Args)], ctypes.c_int),
     "tc_sync": ([ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
+    "tc_stream_create": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "tc_stream_destroy": ([ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
+    "tc_memcpy_htod_on": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64],
+                          ctypes.c_int),
+    "tc_memcpy_dtoh_on": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64],
+                          ctypes.c_int),
+    "tc_event_record_on": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "tc_stream_wait_event": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "tc_event_sync": ([ctypes.c_uint64, ctypes.c_int], ctypes.c_int),
+    "tc_plan_run_on": ([ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
     "tc_event_create": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "tc_event_record": ([ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
     "tc_event_elapsed_ms": ([ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_float)], ctypes.c_int),
@@ -752,3 +762,85 @@ class PinnedHost:
         if self.ptr:
             check(lib().tc_host_free(self.ptr))
             self.ptr = None
+
+
+class StreamedProgram:
+    """A resident program fed from and drained to host memory, copies overlapped across steps.
+
+    `slots` device copies of the program (inputs, arena, outputs) rotate; each `submit` copies one
+    step's inputs in on an input stream, runs the program on the compute stream once they have
+    landed, and copies its outputs out on an output stream -- so step k's outputs travel while step
+    k+1's inputs travel the other way.  Every step still moves all of its own inputs and outputs.
+    """
+
+    def __init__(self, runner, graph, lowered, inputs, outputs, slots=2, capture=True):
+        self.runner = runner
+        self.inputs, self.outputs = list(inputs), list(outputs)
+        self.progs = [Program(runner, graph, lowered, keep=outputs) for _ in range(slots)]
+        if capture:
+            for p in self.progs:
+                p.capture()
+        lib_ = lib()
+        self.s_in, self.s_out = ctypes.c_uint64(), ctypes.c_uint64()
+        check(lib_.tc_stream_create(runner.ctx, ctypes.byref(self.s_in)))
+        check(lib_.tc_stream_create(runner.ctx, ctypes.byref(self.s_out)))
+        self.s_in, self.s_out = self.s_in.value, self.s_out.value
+        self.s_comp = runner.stream()
+        self.ev = Events(runner, 3 * slots + 2)
+        self.slots = slots
+        self.used = [False] * slots
+        self.k = 0
+
+    def _rec(self, k, stream):
+        check(lib().tc_event_record_on(self.runner.ctx, self.ev.ev[k], stream))
+
+    def _wait(self, stream, k):
+        check(lib().tc_stream_wait_event(self.runner.ctx, stream, self.ev.ev[k]))
+
+    def mark(self, which):
+        """Record timing event 0 ('start', on the input stream) or 1 ('end', on the output stream)."""
+        k = 3 * self.slots + (0 if which == "start" else 1)
+        self._rec(k, self.s_in if which == "start" else self.s_out)
+
+    def elapsed_ms(self):
+        return self.ev.ms(3 * self.slots, 3 * self.slots + 1)
+
+    def submit(self, host_in, host_out):
+        """host_in / host_out: {node id: (host pointer, bytes)} for every input and output."""
+        S = self.slots
+        slot = self.k % S
+        p = self.progs[slot]
+        IN, COMP, OUT = 3 * slot, 3 * slot + 1, 3 * slot + 2
+        lib_ = lib()
+        if self.used[slot]:
+            self._wait(self.s_in, COMP)       # the slot's previous step has read its inputs
+        for nid in self.inputs:
+            ptr, n = host_in[nid]
+            check(lib_.tc_memcpy_htod_on(self.runner.ctx, p.ptr(nid), ptr, n, self.s_in))
+        self._rec(IN, self.s_in)
+        self._wait(self.s_comp, IN)
+        if self.used[slot]:
+            self._wait(self.s_comp, OUT)      # ... and its outputs have left
+        check(lib_.tc_plan_run_on(p.plan, self.s_comp))
+        self._rec(COMP, self.s_comp)
+        self._wait(self.s_out, COMP)
+        for nid in self.outputs:
+            ptr, n = host_out[nid]
+            check(lib_.tc_memcpy_dtoh_on(self.runner.ctx, ptr, p.ptr(nid), n, self.s_out))
+        self._rec(OUT, self.s_out)
+        self.used[slot] = True
+        self.k += 1
+
+    def drain(self, timeout_ms=SYNC_TIMEOUT_MS):
+        k = 3 * self.slots + 1
+        self._rec(k, self.s_out)
+        check(lib().tc_event_sync(self.ev.ev[k], timeout_ms))
+
+    def free(self):
+        self.drain()
+        self.runner.sync()
+        for p in self.progs:
+            p.free()
+        self.ev.free()
+        check(lib().tc_stream_destroy(self.runner.ctx, self.s_in))
+        check(lib().tc_stream_destroy(self.runner.ctx, self.s_out))

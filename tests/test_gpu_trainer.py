@@ -102,3 +102,39 @@ def test_folded_transposes_and_aliased_reshapes_change_no_bit(pkg, runner):
             assert np.array_equal(prog.read(k).view(np.uint32), plain["values"][k].view(np.uint32)), k
     finally:
         prog.free()
+
+
+def test_streamed_program_matches_step_by_step(pkg, runner):
+    """Pipelined steps (copies overlapped across steps, two device slots) give each step's own results."""
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    cg = importlib.import_module("tensor-compiler-webgpu_b200.codegen")
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    W = wl.c2_graph(256, 1024)
+    f = pkg.fuse.fuse(W["graph"], keep=W["keep"])
+    low = cg.lower_fused(f.graph)
+    outs = [f.index[k] for k in W["keep"]]
+    ins = [n.id for n in f.graph.inputs()]
+    sp = rt.StreamedProgram(runner, f.graph, low, ins, outs, slots=2)
+    steps, hosts, want = 5, [], []
+    try:
+        for s in range(steps):
+            data = wl.c2_inputs(W, seed=s + 1)
+            hin = {n.id: rt.PinnedHost(data[n.attrs["name"]].nbytes) for n in f.graph.inputs()}
+            for n in f.graph.inputs():
+                hin[n.id].array(data[n.attrs["name"]].size)[:] = data[n.attrs["name"]]
+            hout = {o: rt.PinnedHost(pkg.ir.size(f.graph.nodes[o].shape) * 4) for o in outs}
+            hosts.append((hin, hout))
+            ref = runner.run(f.graph, low, {n.attrs["name"]: data[n.attrs["name"]] for n in f.graph.inputs()})
+            want.append({o: ref["values"][o] for o in outs})
+        for hin, hout in hosts:
+            sp.submit({k: (h.ptr, h.nbytes) for k, h in hin.items()}, {k: (h.ptr, h.nbytes) for k, h in hout.items()})
+        sp.drain()
+        for s, (hin, hout) in enumerate(hosts):
+            for o in outs:
+                got = hout[o].array(hout[o].nbytes // 4)
+                assert np.array_equal(got.view(np.uint32), want[s][o].view(np.uint32)), (s, o)
+    finally:
+        sp.free()
+        for hin, hout in hosts:
+            for h in list(hin.values()) + list(hout.values()):
+                h.free()
