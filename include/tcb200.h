@@ -102,12 +102,12 @@ int tc_module_free(tc_module* mod);
 /* One dispatch (runtime.js:86-101's setPipeline/setBindGroup/dispatchWorkgroups). */
 int tc_launch(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],
               uint32_t smem_bytes, const tc_args* args);
-/* A dispatch of a TMA-fed kernel: up to 4 fp32 tensor maps (128-byte
- * swizzle, zero fill out of bounds) are built from 8 values each --
- * (address, cols, rows, batches, row_stride_bytes, batch_stride_bytes,
- * box_cols, box_rows) -- and passed, 64-byte aligned, before the tc_args
- * block.  The address must be 16-byte aligned, the strides multiples of 16
- * bytes, and box_cols * 4 at most 128. */
+/* A dispatch of a TMA-fed kernel: up to 4 fp32 tensor maps (zero fill out
+ * of bounds) are built from 8 values each -- (address, cols, rows, batches,
+ * row_stride_bytes, batch_stride_bytes, box_cols, box_rows) -- and passed,
+ * 64-byte aligned, before the tc_args block.  The address must be 16-byte
+ * aligned, the strides multiples of 16 bytes, box_cols * 4 one of 128, 64 or
+ * 32 bytes (the swizzle width: 128B, 64B or 32B), box_rows at most 256. */
 int tc_launch_tma(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],
                   uint32_t smem_bytes, int n_maps, const uint64_t* map_desc /* 8 per map */,
                   const tc_args* args);

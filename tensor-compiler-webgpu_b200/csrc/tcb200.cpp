@@ -359,14 +359,19 @@ int encode_maps(int n_maps, const uint64_t* d, TmaBlock* blk) {
     uint64_t addr = v[0], cols = v[1], rows = v[2], batches = v[3], rs = v[4], bs = v[5], bc = v[6], br = v[7];
     if (addr % 16) return fail(TC_ERR_INVALID, "tensor map %d: address not 16-byte aligned", m);
     if (rs % 16 || bs % 16) return fail(TC_ERR_INVALID, "tensor map %d: strides must be multiples of 16 bytes", m);
-    if (bc * 4 > 128 || bc == 0 || br == 0 || br > 256) return fail(TC_ERR_INVALID, "tensor map %d: bad box", m);
+    if ((bc * 4 != 128 && bc * 4 != 64 && bc * 4 != 32) || br == 0 || br > 256)
+      return fail(TC_ERR_INVALID, "tensor map %d: box of %llu x %llu floats", m, (unsigned long long)bc,
+                  (unsigned long long)br);
     if (cols == 0 || rows == 0 || batches == 0) return fail(TC_ERR_INVALID, "tensor map %d: empty", m);
     cuuint64_t dims[3] = {cols, rows, batches};
     cuuint64_t strides[2] = {rs, bs};
     cuuint32_t box[3] = {(cuuint32_t)bc, (cuuint32_t)br, 1};
     cuuint32_t estr[3] = {1, 1, 1};
+    // the swizzle spans one box row: 128, 64 or 32 bytes
+    CUtensorMapSwizzle sw = bc * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                            : bc * 4 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
     CUresult r = CU(cuTensorMapEncodeTiled)(&blk->maps[m], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)addr, dims, strides,
-                                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(TC_ERR_INVALID, "cuTensorMapEncodeTiled (map %d): %s", m, cu_name(r));
   }

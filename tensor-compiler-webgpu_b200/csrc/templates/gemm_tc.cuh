@@ -33,7 +33,12 @@ struct GemmParams {
   Args a;
 };
 
-constexpr int GB_M = 128, GB_K = 32;
+#ifndef TCB_BK
+#define TCB_BK 32
+#endif
+// K-block: 32 fp32 (128-byte rows, 128-byte swizzle) or 16 fp32 (64-byte rows, 64-byte swizzle).
+constexpr int GB_M = 128, GB_K = TCB_BK;
+static_assert(GB_K == 32 || GB_K == 16, "K-block of 16 or 32 floats");
 constexpr u32 WAIT_NS = 2000000000u;  // 2 s: far above any legitimate wait
 
 __device__ __forceinline__ u32 smem_u32(const void* p) { return (u32)__cvta_generic_to_shared(p); }
@@ -70,14 +75,15 @@ __device__ __forceinline__ void tma_load_3d(u32 dst, const TmaDesc* map, u32 bar
       :: "r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
 }
 
-// tcgen05 shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart.
+// tcgen05 shared-memory matrix descriptor, K-major: rows of GB_K floats, 8-row swizzle atoms
+// (1024 B apart with the 128-byte swizzle, 512 B with the 64-byte one).
 __device__ __forceinline__ u64 sw128_desc(u32 saddr) {
   u64 d = 0;
-  d |= (u64)((saddr >> 4) & 0x3FFF);        // start address
-  d |= (u64)1 << 16;                         // leading byte offset (unused for swizzled K-major)
-  d |= (u64)(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
-  d |= (u64)1 << 46;                         // descriptor version for sm_100
-  d |= (u64)2 << 61;                         // 128-byte swizzle
+  d |= (u64)((saddr >> 4) & 0x3FFF);                    // start address
+  d |= (u64)1 << 16;                                     // leading byte offset (unused for swizzled K-major)
+  d |= (u64)((8 * GB_K * 4) >> 4) << 32;                 // stride byte offset: 8 rows
+  d |= (u64)1 << 46;                                     // descriptor version for sm_100
+  d |= (u64)(GB_K == 32 ? 2 : 4) << 61;                  // 128-byte or 64-byte swizzle
   return d;
 }
 

@@ -84,8 +84,17 @@ def fuzz_sources(every=10):
     return codes
 
 
-def warm(full=True):
+def warm(full=True, prune=True):
+    """Compile the standard kernels into the cache; with `prune`, drop cached cubins of other sources
+    (old templates or codegen) so the cache that travels with the tree stays small."""
+    import os
     codes = standard_sources(full)
     if full:
         codes |= sweep_sources() | fuzz_sources(10)
-    return rt.precompile(codes)
+    n = rt.precompile(codes)
+    if prune and full and os.path.isdir(rt.CACHE_DIR):
+        keep = {os.path.basename(rt._cache_path(c)) for c in codes}
+        for name in os.listdir(rt.CACHE_DIR):
+            if name.endswith(".cubin") and name not in keep:
+                os.unlink(os.path.join(rt.CACHE_DIR, name))
+    return n
