@@ -632,7 +632,7 @@ def gemm_stages(bn, bk=32):
 
 def gemm_smem(bn, bk=32):
     st = gemm_stages(bn, bk)
-    return st * gemm_stage_bytes(bn, bk) + (2 * st + 1) * 8 + 16 + 1024
+    return st * gemm_stage_bytes(bn, bk) + (2 * st + 4) * 8 + 16 + 1024
 
 
 def gemm_bk(bn=128):
@@ -683,8 +683,7 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
     err_off = 2 * a_bytes + 2 * b_bytes
     splitk, part_off = splitk_plan(batch, M, K, N, bn)
     scratch = err_off + 256 + (splitk * batch * M * N * 4 if splitk > 1 else 0)
-    if batch * splitk > 65535:
-        raise ValueError("matmul grid too large")
+
     bk = gemm_bk(bn)
     maps = [("scratch", 0, Kp, M, batch, Kp * 4, M * Kp * 4, bk, GEMM_BM),
             ("scratch", a_bytes, Kp, M, batch, Kp * 4, M * Kp * 4, bk, GEMM_BM),
@@ -694,8 +693,8 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
                         else grid1d(batch * M * Kp, per_thread=4), (256, 1, 1)),
              KernelCall("tcb_split_b", grid1d(batch * N * Kp, per_thread=4) if b_t
                         else (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)),
-             KernelCall("tcb_gemm_tc", (math.ceil(N / bn), math.ceil(M / GEMM_BM), batch * splitk), (192, 1, 1),
-                        gemm_smem(bn, bk), [])]
+             KernelCall("tcb_gemm_tc", (min(SM_COUNT, math.ceil(N / bn) * math.ceil(M / GEMM_BM) * batch * splitk), 1, 1),
+                        (192, 1, 1), gemm_smem(bn, bk), [])]
     calls[0].err_offset = err_off
     calls[2].tma = maps
     calls[2].err_offset = err_off

@@ -209,6 +209,8 @@ extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a)
 #endif
 }
 
+// Persistent: one CTA per SM walks the output tiles (grouped raster for L2 reuse); TMEM holds two
+// BN-column accumulators so the epilogue of tile j overlaps the mainloop of tile j+1.
 extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_constant__ tcb::GemmParams P) {
   using namespace tcb;
   constexpr int BN = TCB_BN, STAGES = TCB_STAGES;
@@ -216,32 +218,48 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
   constexpr u32 STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   constexpr u32 KB_ALL = TCB_KP / GB_K;
   constexpr u32 KB_PER = (KB_ALL + TCB_SPLITK - 1) / TCB_SPLITK;  // k-blocks per split
+  constexpr u32 TILES_M = (TCB_M + GB_M - 1) / GB_M, TILES_N = (TCB_N + BN - 1) / BN;
+  constexpr u32 TILES_PER = TILES_M * TILES_N;
+  constexpr u32 TILES = TILES_PER * TCB_BATCH * TCB_SPLITK;
+  constexpr u32 GROUP = 8;
   extern __shared__ unsigned char smem_raw[];
   const u32 raw = smem_u32(smem_raw);
   const u32 base = (raw + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
-  const u32 bars = base + STAGES * STAGE_BYTES;  // full[STAGES], empty[STAGES], accum
-  u32* tmem_slot = reinterpret_cast<u32*>(gbase + STAGES * STAGE_BYTES + (2 * STAGES + 1) * 8);
+  const u32 bars = base + STAGES * STAGE_BYTES;  // full[S], empty[S], accf[2], acce[2]
+  u32* tmem_slot = reinterpret_cast<u32*>(gbase + STAGES * STAGE_BYTES + (2 * STAGES + 4) * 8);
   u32* err = reinterpret_cast<u32*>(P.a.p[15]);  // global error word (may be null)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * GB_M, bz = blockIdx.z / TCB_SPLITK;
-  const u32 split = blockIdx.z % TCB_SPLITK;
-  const u32 kb_begin = split * KB_PER;
-  const u32 kb_end = kb_begin + KB_PER < KB_ALL ? kb_begin + KB_PER : KB_ALL;
-  const u32 KB = kb_end > kb_begin ? kb_end - kb_begin : 0;
   auto full = [&](int s) { return bars + 8u * s; };
   auto empty = [&](int s) { return bars + 8u * (STAGES + s); };
-  const u32 accum = bars + 8u * (2 * STAGES);
+  auto accf = [&](u32 b) { return bars + 8u * (2 * STAGES + b); };
+  auto acce = [&](u32 b) { return bars + 8u * (2 * STAGES + 2 + b); };
+  struct Tile { int m0, n0, bz; u32 kb0, kb; };
+  auto decode = [&](u32 t) {
+    Tile T;
+    const u32 bs = t / TILES_PER, r = t % TILES_PER;
+    T.bz = (int)(bs / TCB_SPLITK);
+    const u32 split = bs % TCB_SPLITK;
+    const u32 group = r / (GROUP * TILES_N), first = group * GROUP;
+    const u32 gsz = TILES_M - first < GROUP ? TILES_M - first : GROUP;
+    const u32 w = r % (GROUP * TILES_N);
+    T.m0 = (int)((first + w % gsz) * GB_M);
+    T.n0 = (int)((w / gsz) * BN);
+    T.kb0 = split * KB_PER;
+    const u32 kb1 = T.kb0 + KB_PER < KB_ALL ? T.kb0 + KB_PER : KB_ALL;
+    T.kb = kb1 > T.kb0 ? kb1 - T.kb0 : 0;
+    return T;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(full(s), 1); mbar_init(empty(s), 1); }
-    mbar_init(accum, 1);
+    for (u32 b = 0; b < 2; ++b) { mbar_init(accf(b), 1); mbar_init(acce(b), 4); }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(smem_u32(tmem_slot)),
-                 "r"((u32)BN) : "memory");
+                 "r"((u32)(2 * BN)) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
@@ -251,90 +269,112 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
 
   if (warp == 0) {
     if (lane == 0) {
-      for (u32 kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES;
-        if (kb >= (u32)STAGES && !mbar_wait(empty(s), ((kb / STAGES) - 1) & 1, err, 1)) break;
-        const u32 st = base + s * STAGE_BYTES;
-        mbar_expect_tx(full(s), STAGE_BYTES);
-        const int kc = (kb_begin + kb) * GB_K;
-        tma_load_3d(st, &P.maps[0], full(s), kc, m0, bz);
-        tma_load_3d(st + A_BYTES, &P.maps[1], full(s), kc, m0, bz);
-        tma_load_3d(st + 2 * A_BYTES, &P.maps[2], full(s), kc, n0, bz);
-        tma_load_3d(st + 2 * A_BYTES + B_BYTES, &P.maps[3], full(s), kc, n0, bz);
+      u32 it = 0;
+      bool ok = true;
+      for (u32 t = blockIdx.x; ok && t < TILES; t += gridDim.x) {
+        const Tile T = decode(t);
+        for (u32 kb = 0; kb < T.kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (it >= (u32)STAGES && !mbar_wait(empty(s), ((it / STAGES) - 1) & 1, err, 1)) { ok = false; break; }
+          const u32 st = base + s * STAGE_BYTES;
+          mbar_expect_tx(full(s), STAGE_BYTES);
+          const int kc = (int)((T.kb0 + kb) * GB_K);
+          tma_load_3d(st, &P.maps[0], full(s), kc, T.m0, T.bz);
+          tma_load_3d(st + A_BYTES, &P.maps[1], full(s), kc, T.m0, T.bz);
+          tma_load_3d(st + 2 * A_BYTES, &P.maps[2], full(s), kc, T.n0, T.bz);
+          tma_load_3d(st + 2 * A_BYTES + B_BYTES, &P.maps[3], full(s), kc, T.n0, T.bz);
+        }
       }
       // drain: wait (bounded) for the copies still in flight before this CTA may exit
-      for (u32 kb = KB > (u32)STAGES ? KB - STAGES : 0; kb < KB; ++kb)
-        mbar_wait(full(kb % STAGES), (kb / STAGES) & 1, err, 2);
+      for (u32 i = it > (u32)STAGES ? it - STAGES : 0; i < it; ++i) mbar_wait(full(i % STAGES), (i / STAGES) & 1, err, 2);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr u32 ID = idesc_tf32(BN);
-      for (u32 kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES;
-        if (!mbar_wait(full(s), (kb / STAGES) & 1, err, 3)) break;
+      u32 it = 0, j = 0;
+      bool ok = true;
+      for (u32 t = blockIdx.x; ok && t < TILES; t += gridDim.x, ++j) {
+        const Tile T = decode(t);
+        const u32 buf = j & 1;
+        if (j >= 2 && !mbar_wait(acce(buf), ((j >> 1) - 1) & 1, err, 5)) break;
         tc_fence_after();
-        const u32 st = base + s * STAGE_BYTES;
+        const u32 acc = tmem + buf * BN;
+        for (u32 kb = 0; kb < T.kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(full(s), (it / STAGES) & 1, err, 3)) { ok = false; break; }
+          tc_fence_after();
+          const u32 st = base + s * STAGE_BYTES;
 #pragma unroll
-        for (int k = 0; k < GB_K / 8; ++k) {
-          const u64 ah = sw128_desc(st + 32 * k), al = sw128_desc(st + A_BYTES + 32 * k);
-          const u64 bh = sw128_desc(st + 2 * A_BYTES + 32 * k), bl = sw128_desc(st + 2 * A_BYTES + B_BYTES + 32 * k);
-          mma_tf32(tmem, al, bh, ID, (kb | k) != 0);
-          mma_tf32(tmem, ah, bl, ID, 1);
-          mma_tf32(tmem, ah, bh, ID, 1);
+          for (int k = 0; k < GB_K / 8; ++k) {
+            const u64 ah = sw128_desc(st + 32 * k), al = sw128_desc(st + A_BYTES + 32 * k);
+            const u64 bh = sw128_desc(st + 2 * A_BYTES + 32 * k), bl = sw128_desc(st + 2 * A_BYTES + B_BYTES + 32 * k);
+            mma_tf32(acc, al, bh, ID, (kb | k) != 0);
+            mma_tf32(acc, ah, bl, ID, 1);
+            mma_tf32(acc, ah, bh, ID, 1);
+          }
+          mma_commit(empty(s));
         }
-        mma_commit(empty(s));
+        mma_commit(accf(buf));  // with no k-block in this split the accumulator is never enabled: see the epilogue
       }
-      mma_commit(accum);  // with no k-block in this split the accumulator is never enabled: see the epilogue
     }
   } else {
     // epilogue: warps 2..5 -> TMEM lane quarter (warp % 4)
     const int q = warp & 3;
-    const bool ok = mbar_wait(accum, 0, err, 4);
-    tc_fence_after();
-    const u64 row = (u64)m0 + 32 * q + lane;
     float* __restrict__ out = reinterpret_cast<float*>(P.a.out);
-    if (ok) {
+    u32 j = 0;
+    for (u32 t = blockIdx.x; t < TILES; t += gridDim.x, ++j) {
+      const Tile T = decode(t);
+      const u32 buf = j & 1;
+      if (!mbar_wait(accf(buf), (j >> 1) & 1, err, 4)) break;
+      tc_fence_after();
+      const u64 row = (u64)T.m0 + 32 * q + lane;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
-        tmem_ld16(tmem + ((u32)(32 * q) << 16) + (u32)c0, v);
-        if (KB == 0) {
+        tmem_ld16(tmem + buf * BN + ((u32)(32 * q) << 16) + (u32)c0, v);
+        if (T.kb == 0) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+          for (int jj = 0; jj < 16; ++jj) v[jj] = 0.0f;
         }
         if (TCB_SPLITK > 1) {
           // partial sums of this split: [SPLITK][batch][M][N] floats after the split operands in scratch
           if (row < (u64)TCB_M) {
+            const u64 split = (t / TILES_PER) % TCB_SPLITK;
             float* part = reinterpret_cast<float*>(P.a.scratch) + TCB_PART_OFFSET / 4 +
-                          (((u64)split * TCB_BATCH + bz) * TCB_M + row) * TCB_N;
-            for (int j = 0; j < 16; ++j)
-              if ((u64)(n0 + c0 + j) < (u64)TCB_N) part[n0 + c0 + j] = v[j];
+                          ((split * TCB_BATCH + (u64)T.bz) * TCB_M + row) * TCB_N;
+            for (int jj = 0; jj < 16; ++jj)
+              if ((u64)(T.n0 + c0 + jj) < (u64)TCB_N) part[T.n0 + c0 + jj] = v[jj];
           }
           continue;
         }
-        if (row < (u64)TCB_M && (u64)(n0 + c0) < (u64)TCB_N) {
-          const u64 base_i = (u64)bz * TCB_M * TCB_N + row * TCB_N + (u64)(n0 + c0);
+        if (row < (u64)TCB_M && (u64)(T.n0 + c0) < (u64)TCB_N) {
+          const u64 base_i = (u64)T.bz * TCB_M * TCB_N + row * TCB_N + (u64)(T.n0 + c0);
           float o[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const u64 col = (u64)(n0 + c0 + j);
-            o[j] = col < (u64)TCB_N ? Epi::apply(P.a, v[j], base_i + j, row, col, (u64)bz) : 0.0f;
+          for (int jj = 0; jj < 16; ++jj) {
+            const u64 col = (u64)(T.n0 + c0 + jj);
+            o[jj] = col < (u64)TCB_N ? Epi::apply(P.a, v[jj], base_i + jj, row, col, (u64)T.bz) : 0.0f;
           }
-          if ((TCB_N % 4) == 0 && (u64)(n0 + c0 + 16) <= (u64)TCB_N) {
+          if ((TCB_N % 4) == 0 && (u64)(T.n0 + c0 + 16) <= (u64)TCB_N) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(out + base_i + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+            for (int jj = 0; jj < 16; jj += 4)
+              *reinterpret_cast<float4*>(out + base_i + jj) = make_float4(o[jj], o[jj + 1], o[jj + 2], o[jj + 3]);
           } else {
-            for (int j = 0; j < 16; ++j) if ((u64)(n0 + c0 + j) < (u64)TCB_N) out[base_i + j] = o[j];
+            for (int jj = 0; jj < 16; ++jj) if ((u64)(T.n0 + c0 + jj) < (u64)TCB_N) out[base_i + jj] = o[jj];
           }
         }
       }
+      // this warp's reads of the accumulator are complete: hand the buffer back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(acce(buf)) : "memory");
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"((u32)BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"((u32)(2 * BN)) : "memory");
   }
 }
 
