@@ -366,8 +366,16 @@ def _tf32x3_peak():
 
 
 def _code_hash(code):
+    """Hash of a launch's source plus the text of every library template it includes, so a
+    recorded traffic figure is used only for the exact kernel it was captured on."""
     import hashlib
-    return hashlib.sha256(code.encode()).hexdigest()[:16]
+    import re
+    h = hashlib.sha256(code.encode())
+    tdir = os.path.join(ROOT, "tensor-compiler-webgpu_b200", "csrc", "templates")
+    for name in sorted(set(re.findall(r'#include "tcb/([a-z_]+\.cuh)"', code))):
+        with open(os.path.join(tdir, name), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
 
 
 def cpu_baseline(name, pkg, cg, wl, seconds):

@@ -587,9 +587,12 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=Fa
     if kernel == "tcgen05":
         splitk, part_off = splitk_plan(batch, M, K, N, bn)
         bk = gemm_bk(bn)
+        grid, tail, cnt_off, tail_off, _ = tail_plan(batch, M, K, N, bn, bk, splitk)
         tc_defs = (f"#define TCB_KP {_kpad(K)}\n#define TCB_BN {bn}\n#define TCB_BK {bk}\n"
                    f"#define TCB_STAGES {gemm_stages(bn, bk)}\n"
                    f"#define TCB_SPLITK {splitk}\n#define TCB_PART_OFFSET {part_off}ull\n"
+                   f"#define TCB_GRID {grid}\n#define TCB_TAIL_SPLIT {tail}\n"
+                   f"#define TCB_TAIL_CNT_OFFSET {cnt_off}ull\n#define TCB_TAIL_OFFSET {tail_off}ull\n"
                    f"#define TCB_A_T {int(a_t)}\n#define TCB_B_T {int(b_t)}\n")
     src = f"""// matmul epilogue ({kernel}): batch {batch}, [{M},{K}] x [{K},{N}]
 #include "tcb/common.cuh"
@@ -661,6 +664,29 @@ def splitk_plan(batch, M, K, N, bn):
     return s, part_off
 
 
+def tail_plan(batch, M, K, N, bn, bk, splitk):
+    """The persistent GEMM's grid and last-wave split.
+
+    Returns (grid, tail, cnt_off, tail_off, scratch_end): grid = min(SMs, tiles) CTAs; when the last
+    wave would hold rem <= grid/2 tiles, each of them is cut into `tail` K ranges (>= 4 k-blocks each,
+    at most 8) so that wave fills the SMs.  Their arrival counters (4 per tile) sit at cnt_off and
+    their partial tiles (128 x bn floats per range) at tail_off in scratch; scratch_end is the end of
+    that region (0 when there is no split).
+    """
+    tiles = batch * math.ceil(M / GEMM_BM) * math.ceil(N / bn) * splitk
+    grid = min(SM_COUNT, tiles)
+    rem = tiles % grid
+    tail = 1
+    if splitk == 1 and rem and 2 * rem <= grid:
+        tail = min(grid // rem, (_kpad(K) // bk) // 4, 8)
+    if tail < 2:
+        return grid, 1, 0, 0, 0
+    Kp = _kpad(K)
+    cnt_off = 2 * batch * M * Kp * 4 + 2 * batch * N * Kp * 4 + 256
+    tail_off = cnt_off + (4 * rem * 4 + 255) // 256 * 256
+    return grid, tail, cnt_off, tail_off, tail_off + rem * tail * GEMM_BM * bn * 4
+
+
 def gemm_bn(N):
     """Accumulator width: 256 TMEM columns when N fills them, else 128."""
     import os
@@ -682,9 +708,10 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
     b_bytes = batch * N * Kp * 4
     err_off = 2 * a_bytes + 2 * b_bytes
     splitk, part_off = splitk_plan(batch, M, K, N, bn)
-    scratch = err_off + 256 + (splitk * batch * M * N * 4 if splitk > 1 else 0)
-
     bk = gemm_bk(bn)
+    grid, tail, _, _, tail_end = tail_plan(batch, M, K, N, bn, bk, splitk)
+    scratch = max(err_off + 256 + (splitk * batch * M * N * 4 if splitk > 1 else 0), tail_end)
+
     maps = [("scratch", 0, Kp, M, batch, Kp * 4, M * Kp * 4, bk, GEMM_BM),
             ("scratch", a_bytes, Kp, M, batch, Kp * 4, M * Kp * 4, bk, GEMM_BM),
             ("scratch", 2 * a_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn),
@@ -693,8 +720,7 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
                         else grid1d(batch * M * Kp, per_thread=4), (256, 1, 1)),
              KernelCall("tcb_split_b", grid1d(batch * N * Kp, per_thread=4) if b_t
                         else (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)),
-             KernelCall("tcb_gemm_tc", (min(SM_COUNT, math.ceil(N / bn) * math.ceil(M / GEMM_BM) * batch * splitk), 1, 1),
-                        (192, 1, 1), gemm_smem(bn, bk), [])]
+             KernelCall("tcb_gemm_tc", (grid, 1, 1), (192, 1, 1), gemm_smem(bn, bk), [])]
     calls[0].err_offset = err_off
     calls[2].tma = maps
     calls[2].err_offset = err_off
@@ -702,7 +728,7 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
         calls.append(KernelCall("tcb_splitk_finish", grid1d(batch * M * N, per_thread=1), (256, 1, 1)))
     lau = Launch(node_id, op, kind, pattern, inputs, code, calls, scratch_bytes=scratch,
                  info={"mnk": (batch, M, K, N), "bn": bn, "bk": bk, "stages": gemm_stages(bn, bk), "splitk": splitk,
-                       "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t})
+                       "tail_split": tail, "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t})
     return lau
 
 

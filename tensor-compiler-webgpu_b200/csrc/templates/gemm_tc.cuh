@@ -39,7 +39,10 @@ struct GemmParams {
 // K-block: 32 fp32 (128-byte rows, 128-byte swizzle) or 16 fp32 (64-byte rows, 64-byte swizzle).
 constexpr int GB_M = 128, GB_K = TCB_BK;
 static_assert(GB_K == 32 || GB_K == 16, "K-block of 16 or 32 floats");
-constexpr u32 WAIT_NS = 2000000000u;  // 2 s: far above any legitimate wait
+#ifndef TCB_WAIT_NS
+#define TCB_WAIT_NS 2000000000u  // 2 s: far above any legitimate wait
+#endif
+constexpr u32 WAIT_NS = TCB_WAIT_NS;
 
 __device__ __forceinline__ u32 smem_u32(const void* p) { return (u32)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ u64 now_ns() { u64 t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; }
@@ -132,8 +135,42 @@ __device__ __forceinline__ float tf32_rna(float x) {
 #ifndef TCB_B_T
 #define TCB_B_T 0   // 1: operand B arrives as its transpose Y [batch, N, K]
 #endif
+#ifndef TCB_PART_OFFSET
+#define TCB_PART_OFFSET 0ull
+#endif
+#ifndef TCB_GRID
+#define TCB_GRID 148
+#endif
+#ifndef TCB_TAIL_SPLIT
+#define TCB_TAIL_SPLIT 1
+#endif
+#ifndef TCB_TAIL_OFFSET
+#define TCB_TAIL_OFFSET 0ull
+#endif
+#ifndef TCB_TAIL_CNT_OFFSET
+#define TCB_TAIL_CNT_OFFSET 0ull
+#endif
 
 namespace tcb {
+// Work units of the persistent GEMM (TCB_GRID CTAs, unit u on CTA u % GRID).  Units below U_FULL are
+// whole output tiles (of one K split).  When the last wave would hold only REM <= GRID/2 tiles, each
+// of those tiles becomes TAIL units over equal K ranges instead, so the last wave fills the SMs; their
+// partial tiles meet in scratch and the warp that finishes a tile's quarter last reduces it, adding the
+// partials in unit order (so the result does not depend on which CTA came last).
+struct GemmShape {
+  static constexpr u32 KB_ALL = TCB_KP / GB_K;
+  static constexpr u32 TILES_M = (TCB_M + GB_M - 1) / GB_M, TILES_N = (TCB_N + TCB_BN - 1) / TCB_BN;
+  static constexpr u32 TILES_PER = TILES_M * TILES_N;
+  static constexpr u32 TILES = TILES_PER * TCB_BATCH * TCB_SPLITK;
+  static constexpr u32 GRID = TCB_GRID;
+  static constexpr u32 TAIL = TCB_TAIL_SPLIT;
+  static constexpr u32 REM = TAIL > 1 ? TILES % GRID : 0;
+  static constexpr u32 U_FULL = TILES - REM;
+  static constexpr u32 UNITS = U_FULL + REM * TAIL;
+};
+static_assert(TCB_TAIL_SPLIT == 1 || TCB_SPLITK == 1, "tail split and split-K are exclusive");
+static_assert(TCB_TAIL_SPLIT <= GemmShape::KB_ALL, "every tail unit has at least one k-block");
+
 // Row-major src [batch, R, C] -> hi, lo [batch, R, Kp] with Kp >= C (zero beyond C), 4 elements per step.
 __device__ __forceinline__ void split_rows(const float* __restrict__ src, float* __restrict__ hi, float* __restrict__ lo,
                                            u64 rows, u64 C, u64 Kp) {
@@ -185,8 +222,12 @@ __device__ __forceinline__ void split_cols(const float* __restrict__ src, float*
 // A -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.  It runs first in every tensor-core
 // launch, so it also clears that launch's error word (p[15]) in the reused scratch.
 extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a) {
-  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0 && a.p[15])
-    *reinterpret_cast<u32*>(a.p[15]) = 0u;
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+    if (threadIdx.x == 0 && a.p[15]) *reinterpret_cast<u32*>(a.p[15]) = 0u;
+    // the tail units' arrival counters (one per tail tile and TMEM lane quarter)
+    u32* cnt = reinterpret_cast<u32*>(reinterpret_cast<unsigned char*>(a.scratch) + TCB_TAIL_CNT_OFFSET);
+    for (u32 i = threadIdx.x; i < 4 * tcb::GemmShape::REM; i += blockDim.x) cnt[i] = 0u;
+  }
   float* hi = reinterpret_cast<float*>(a.scratch);
   float* lo = hi + (u64)TCB_BATCH * TCB_M * TCB_KP;
   const float* src = reinterpret_cast<const float*>(a.in[TCB_IA]);
@@ -209,46 +250,62 @@ extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a)
 #endif
 }
 
-// Persistent: one CTA per SM walks the output tiles (grouped raster for L2 reuse); TMEM holds two
-// BN-column accumulators so the epilogue of tile j overlaps the mainloop of tile j+1.
+// Persistent: TCB_GRID CTAs (one per SM) walk the work units (grouped raster for L2 reuse); TMEM holds
+// two BN-column accumulators so the epilogue of unit j overlaps the mainloop of unit j+1.
 extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_constant__ tcb::GemmParams P) {
   using namespace tcb;
+  using S = GemmShape;
   constexpr int BN = TCB_BN, STAGES = TCB_STAGES;
   constexpr u32 A_BYTES = GB_M * GB_K * 4, B_BYTES = BN * GB_K * 4;
   constexpr u32 STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-  constexpr u32 KB_ALL = TCB_KP / GB_K;
-  constexpr u32 KB_PER = (KB_ALL + TCB_SPLITK - 1) / TCB_SPLITK;  // k-blocks per split
-  constexpr u32 TILES_M = (TCB_M + GB_M - 1) / GB_M, TILES_N = (TCB_N + BN - 1) / BN;
-  constexpr u32 TILES_PER = TILES_M * TILES_N;
-  constexpr u32 TILES = TILES_PER * TCB_BATCH * TCB_SPLITK;
+  constexpr u32 KB_PER = (S::KB_ALL + TCB_SPLITK - 1) / TCB_SPLITK;  // k-blocks per split
   constexpr u32 GROUP = 8;
+  constexpr u64 CHUNK = (u64)GB_M * 16;                    // floats of one 16-column slice of a partial tile
   extern __shared__ unsigned char smem_raw[];
+  u32* err = reinterpret_cast<u32*>(P.a.p[15]);  // global error word (may be null)
+  if (gridDim.x != S::GRID) {                     // the unit schedule assumes exactly GRID CTAs
+    if (threadIdx.x == 0 && err) atomicCAS(err, 0u, 9u);
+    return;
+  }
   const u32 raw = smem_u32(smem_raw);
   const u32 base = (raw + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
   const u32 bars = base + STAGES * STAGE_BYTES;  // full[S], empty[S], accf[2], acce[2]
   u32* tmem_slot = reinterpret_cast<u32*>(gbase + STAGES * STAGE_BYTES + (2 * STAGES + 4) * 8);
-  u32* err = reinterpret_cast<u32*>(P.a.p[15]);  // global error word (may be null)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto full = [&](int s) { return bars + 8u * s; };
   auto empty = [&](int s) { return bars + 8u * (STAGES + s); };
   auto accf = [&](u32 b) { return bars + 8u * (2 * STAGES + b); };
   auto acce = [&](u32 b) { return bars + 8u * (2 * STAGES + 2 + b); };
-  struct Tile { int m0, n0, bz; u32 kb0, kb; };
-  auto decode = [&](u32 t) {
+  struct Tile { int m0, n0, bz; u32 kb0, kb; int tail; u32 piece; };
+  auto decode = [&](u32 u) {
     Tile T;
-    const u32 bs = t / TILES_PER, r = t % TILES_PER;
+    u32 t = u;
+    T.tail = -1;
+    T.piece = 0;
+    if (u >= S::U_FULL) {  // a K range of a last-wave tile
+      const u32 v = u - S::U_FULL;
+      T.tail = (int)(v / S::TAIL);
+      T.piece = v % S::TAIL;
+      t = S::U_FULL + v / S::TAIL;
+    }
+    const u32 bs = t / S::TILES_PER, r = t % S::TILES_PER;
     T.bz = (int)(bs / TCB_SPLITK);
     const u32 split = bs % TCB_SPLITK;
-    const u32 group = r / (GROUP * TILES_N), first = group * GROUP;
-    const u32 gsz = TILES_M - first < GROUP ? TILES_M - first : GROUP;
-    const u32 w = r % (GROUP * TILES_N);
+    const u32 group = r / (GROUP * S::TILES_N), first = group * GROUP;
+    const u32 gsz = S::TILES_M - first < GROUP ? S::TILES_M - first : GROUP;
+    const u32 w = r % (GROUP * S::TILES_N);
     T.m0 = (int)((first + w % gsz) * GB_M);
     T.n0 = (int)((w / gsz) * BN);
-    T.kb0 = split * KB_PER;
-    const u32 kb1 = T.kb0 + KB_PER < KB_ALL ? T.kb0 + KB_PER : KB_ALL;
-    T.kb = kb1 > T.kb0 ? kb1 - T.kb0 : 0;
+    if (T.tail >= 0) {
+      T.kb0 = T.piece * S::KB_ALL / S::TAIL;
+      T.kb = (T.piece + 1) * S::KB_ALL / S::TAIL - T.kb0;
+    } else {
+      T.kb0 = split * KB_PER;
+      const u32 kb1 = T.kb0 + KB_PER < S::KB_ALL ? T.kb0 + KB_PER : S::KB_ALL;
+      T.kb = kb1 > T.kb0 ? kb1 - T.kb0 : 0;
+    }
     return T;
   };
 
@@ -271,7 +328,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
     if (lane == 0) {
       u32 it = 0;
       bool ok = true;
-      for (u32 t = blockIdx.x; ok && t < TILES; t += gridDim.x) {
+      for (u32 t = blockIdx.x; ok && t < S::UNITS; t += S::GRID) {
         const Tile T = decode(t);
         for (u32 kb = 0; kb < T.kb; ++kb, ++it) {
           const int s = it % STAGES;
@@ -293,7 +350,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
       constexpr u32 ID = idesc_tf32(BN);
       u32 it = 0, j = 0;
       bool ok = true;
-      for (u32 t = blockIdx.x; ok && t < TILES; t += gridDim.x, ++j) {
+      for (u32 t = blockIdx.x; ok && t < S::UNITS; t += S::GRID, ++j) {
         const Tile T = decode(t);
         const u32 buf = j & 1;
         if (j >= 2 && !mbar_wait(acce(buf), ((j >> 1) - 1) & 1, err, 5)) break;
@@ -321,13 +378,82 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
     // epilogue: warps 2..5 -> TMEM lane quarter (warp % 4)
     const int q = warp & 3;
     float* __restrict__ out = reinterpret_cast<float*>(P.a.out);
+    unsigned char* scr = reinterpret_cast<unsigned char*>(P.a.scratch);
+    // the fused body on 16 accumulator values of one row, stored to the output
+    auto finish16 = [&](const Tile& T, u64 row, int c0, float (&v)[16]) {
+      if (row >= (u64)TCB_M || (u64)(T.n0 + c0) >= (u64)TCB_N) return;
+      const u64 base_i = (u64)T.bz * TCB_M * TCB_N + row * TCB_N + (u64)(T.n0 + c0);
+      float o[16];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const u64 col = (u64)(T.n0 + c0 + jj);
+        o[jj] = col < (u64)TCB_N ? Epi::apply(P.a, v[jj], base_i + jj, row, col, (u64)T.bz) : 0.0f;
+      }
+      if ((TCB_N % 4) == 0 && (u64)(T.n0 + c0 + 16) <= (u64)TCB_N) {
+#pragma unroll
+        for (int jj = 0; jj < 16; jj += 4)
+          *reinterpret_cast<float4*>(out + base_i + jj) = make_float4(o[jj], o[jj + 1], o[jj + 2], o[jj + 3]);
+      } else {
+        for (int jj = 0; jj < 16; ++jj) if ((u64)(T.n0 + c0 + jj) < (u64)TCB_N) out[base_i + jj] = o[jj];
+      }
+    };
     u32 j = 0;
-    for (u32 t = blockIdx.x; t < TILES; t += gridDim.x, ++j) {
+    for (u32 t = blockIdx.x; t < S::UNITS; t += S::GRID, ++j) {
       const Tile T = decode(t);
       const u32 buf = j & 1;
       if (!mbar_wait(accf(buf), (j >> 1) & 1, err, 4)) break;
       tc_fence_after();
       const u64 row = (u64)T.m0 + 32 * q + lane;
+      if (S::TAIL > 1 && T.tail >= 0) {
+        // partial tiles in scratch: [tail tile][piece][BN/16 slices][128 rows][16], one 64-byte run per row
+        float* tp = reinterpret_cast<float*>(scr + TCB_TAIL_OFFSET) + (u64)T.tail * S::TAIL * (BN / 16) * CHUNK +
+                    (u64)(32 * q + lane) * 16;
+        float* mine = tp + (u64)T.piece * (BN / 16) * CHUNK;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(tmem + buf * BN + ((u32)(32 * q) << 16) + (u32)c0, v);
+          float4* d = reinterpret_cast<float4*>(mine + (u64)(c0 / 16) * CHUNK);
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) d[jj] = make_float4(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(acce(buf)) : "memory");
+        // publish this warp's rows, then count the arrival; the last of the TAIL pieces reduces them
+        __threadfence();
+        __syncwarp();
+        u32 old = 0;
+        if (lane == 0)
+          old = atomicAdd(reinterpret_cast<u32*>(scr + TCB_TAIL_CNT_OFFSET) + 4 * (u32)T.tail + (u32)q, 1u);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == S::TAIL - 1) {
+          __threadfence();
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            const float* src = tp + (u64)(c0 / 16) * CHUNK;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              const float4 x = __ldcg(reinterpret_cast<const float4*>(src) + jj);
+              v[4 * jj] = x.x; v[4 * jj + 1] = x.y; v[4 * jj + 2] = x.z; v[4 * jj + 3] = x.w;
+            }
+#pragma unroll 1
+            for (u32 pc = 1; pc < S::TAIL; ++pc) {
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                const float4 x = __ldcg(reinterpret_cast<const float4*>(src + (u64)pc * (BN / 16) * CHUNK) + jj);
+                v[4 * jj] = op_add(v[4 * jj], x.x);
+                v[4 * jj + 1] = op_add(v[4 * jj + 1], x.y);
+                v[4 * jj + 2] = op_add(v[4 * jj + 2], x.z);
+                v[4 * jj + 3] = op_add(v[4 * jj + 3], x.w);
+              }
+            }
+            finish16(T, row, c0, v);
+          }
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
@@ -339,7 +465,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
         if (TCB_SPLITK > 1) {
           // partial sums of this split: [SPLITK][batch][M][N] floats after the split operands in scratch
           if (row < (u64)TCB_M) {
-            const u64 split = (t / TILES_PER) % TCB_SPLITK;
+            const u64 split = (t / S::TILES_PER) % TCB_SPLITK;
             float* part = reinterpret_cast<float*>(P.a.scratch) + TCB_PART_OFFSET / 4 +
                           ((split * TCB_BATCH + (u64)T.bz) * TCB_M + row) * TCB_N;
             for (int jj = 0; jj < 16; ++jj)
@@ -347,22 +473,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
           }
           continue;
         }
-        if (row < (u64)TCB_M && (u64)(T.n0 + c0) < (u64)TCB_N) {
-          const u64 base_i = (u64)T.bz * TCB_M * TCB_N + row * TCB_N + (u64)(T.n0 + c0);
-          float o[16];
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const u64 col = (u64)(T.n0 + c0 + jj);
-            o[jj] = col < (u64)TCB_N ? Epi::apply(P.a, v[jj], base_i + jj, row, col, (u64)T.bz) : 0.0f;
-          }
-          if ((TCB_N % 4) == 0 && (u64)(T.n0 + c0 + 16) <= (u64)TCB_N) {
-#pragma unroll
-            for (int jj = 0; jj < 16; jj += 4)
-              *reinterpret_cast<float4*>(out + base_i + jj) = make_float4(o[jj], o[jj + 1], o[jj + 2], o[jj + 3]);
-          } else {
-            for (int jj = 0; jj < 16; ++jj) if ((u64)(T.n0 + c0 + jj) < (u64)TCB_N) out[base_i + jj] = o[jj];
-          }
-        }
+        finish16(T, row, c0, v);
       }
       // this warp's reads of the accumulator are complete: hand the buffer back to the MMA warp
       tc_fence_before();

@@ -102,3 +102,42 @@ def test_transpose_folding_picks_only_gemm_operand_transposes(pkg, cg):
     assert [l.info.get("b_t") for l in mm] == [True, False]
     assert mm[0].inputs == [a, w]
     assert cg.foldable_transposes(g, "naive") == set()   # CUDA-core path: nothing folds
+
+
+@pytest.mark.parametrize("shape", [(1, 4096, 4096, 4096), (1, 16384, 1024, 4096), (198, 128, 256, 128),
+                                   (1, 5120, 256, 1024), (1, 2432, 128, 2048), (2048, 256, 64, 256),
+                                   (1, 256, 131072, 768), (3, 300, 96, 500)])
+def test_gemm_last_wave_plan(cg, shape):
+    """The persistent GEMM's unit schedule: every (tile, k-block) is covered exactly once, the last wave
+    is split only when it would leave at least half the CTAs idle, and no CTA gets more than one
+    unit beyond the full waves."""
+    batch, M, K, N = shape
+    bn = cg.gemm_bn(N)
+    bk = cg.gemm_bk(bn)
+    splitk, _ = cg.splitk_plan(batch, M, K, N, bn)
+    grid, tail, cnt_off, tail_off, end = cg.tail_plan(batch, M, K, N, bn, bk, splitk)
+    tiles = batch * -(-M // cg.GEMM_BM) * -(-N // bn) * splitk
+    assert grid == min(cg.SM_COUNT, tiles)
+    kb_all = cg._kpad(K) // bk
+    rem = tiles % grid if tail > 1 else 0
+    u_full = tiles - rem
+    units = u_full + rem * tail
+    covered = {}
+    for u in range(units):
+        if u < u_full:
+            t, kb0, kb1 = u, 0, kb_all
+        else:
+            v = u - u_full
+            t, p = u_full + v // tail, v % tail
+            kb0, kb1 = p * kb_all // tail, (p + 1) * kb_all // tail
+        assert kb1 > kb0
+        covered.setdefault(t, []).append((kb0, kb1))
+    assert sorted(covered) == list(range(tiles))
+    for rngs in covered.values():
+        assert rngs[0][0] == 0 and rngs[-1][1] == kb_all
+        assert all(a[1] == b[0] for a, b in zip(rngs, rngs[1:]))
+    per_cta = [len(range(c, units, grid)) for c in range(grid)]
+    assert max(per_cta) - min(per_cta) <= 1
+    if tail > 1:
+        assert splitk == 1 and 2 * rem <= grid and kb_all // tail >= 4
+        assert tail_off >= cnt_off + 16 * rem and end == tail_off + rem * tail * cg.GEMM_BM * bn * 4
