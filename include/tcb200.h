@@ -107,7 +107,10 @@ int tc_launch(tc_module* mod, const char* kernel, const uint32_t grid[3], const 
  * row_stride_bytes, batch_stride_bytes, box_cols, box_rows) -- and passed,
  * 64-byte aligned, before the tc_args block.  The address must be 16-byte
  * aligned, the strides multiples of 16 bytes, box_cols * 4 one of 128, 64 or
- * 32 bytes (the swizzle width: 128B, 64B or 32B), box_rows at most 256. */
+ * 32 bytes (the swizzle width: 128B, 64B or 32B), box_rows at most 256.
+ * Bit 32 of box_cols (with 32 floats in its low bits) asks for the 128-byte
+ * swizzle of 32-byte chunks instead: the shared-memory layout the tensor cores
+ * read an MN-major tf32 operand tile in. */
 int tc_launch_tma(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],
                   uint32_t smem_bytes, int n_maps, const uint64_t* map_desc /* 8 per map */,
                   const tc_args* args);

@@ -585,10 +585,13 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=Fa
     code = "\n    ".join(lines)
     tc_defs = ""
     if kernel == "tcgen05":
-        splitk, part_off = splitk_plan(batch, M, K, N, bn)
+        fs = fused_split_plan(batch, M, K, N, bn, a_t, b_t)
+        splitk, part_off = splitk_plan(batch, M, K, N, bn, fs)
         bk = gemm_bk(bn)
-        grid, tail, cnt_off, tail_off, _ = tail_plan(batch, M, K, N, bn, bk, splitk)
+        grid, tail, cnt_off, tail_off, _ = tail_plan(batch, M, K, N, bn, bk, splitk, fs)
         tc_defs = (f"#define TCB_KP {_kpad(K)}\n#define TCB_BN {bn}\n#define TCB_BK {bk}\n"
+                   f"#define TCB_FS_A {int(fs[0])}\n#define TCB_FS_B {int(fs[1])}\n"
+                   f"#define TCB_SPLIT_B_OFFSET {0 if fs[0] else 2 * batch * M * _kpad(K) * 4}ull\n"
                    f"#define TCB_STAGES {gemm_stages(bn, bk)}\n"
                    f"#define TCB_SPLITK {splitk}\n#define TCB_PART_OFFSET {part_off}ull\n"
                    f"#define TCB_GRID {grid}\n#define TCB_TAIL_SPLIT {tail}\n"
@@ -619,6 +622,7 @@ TC_MIN_K = 32    # below this the 3xTF32 split error could exceed gamma_K's shar
 GEMM_BM = 128
 SMEM_LIMIT = 227 * 1024
 KPAD = 32   # K is padded to a multiple of 32 in the split operands whatever the K-block
+TMA_ATOM32 = 1 << 32   # box_cols flag: 128-byte swizzle of 32-byte chunks (MN-major tf32 tiles)
 
 
 def _kpad(K):
@@ -635,7 +639,7 @@ def gemm_stages(bn, bk=32):
 
 def gemm_smem(bn, bk=32):
     st = gemm_stages(bn, bk)
-    return st * gemm_stage_bytes(bn, bk) + (2 * st + 4) * 8 + 16 + 1024
+    return st * gemm_stage_bytes(bn, bk) + (3 * st + 4) * 8 + 16 + 1024
 
 
 def gemm_bk(bn=128):
@@ -648,7 +652,14 @@ def gemm_bk(bn=128):
     return 16 if bn == 256 else 32
 
 
-def splitk_plan(batch, M, K, N, bn):
+def split_bytes(batch, M, K, N, fs=(False, False)):
+    """Scratch taken by the split operands (A_hi, A_lo, then B_hi, B_lo), leaving out an operand the
+    GEMM splits itself (fs = (fa, fb))."""
+    Kp = _kpad(K)
+    return (0 if fs[0] else 2 * batch * M * Kp * 4) + (0 if fs[1] else 2 * batch * N * Kp * 4)
+
+
+def splitk_plan(batch, M, K, N, bn, fs=(False, False)):
     """K splits so that short, wide-K contractions (weight gradients) still cover the SMs.
 
     Returns (splits, byte offset of the partial sums in scratch).  Each split keeps >= 4 k-blocks.
@@ -659,12 +670,11 @@ def splitk_plan(batch, M, K, N, bn):
     if tiles < SM_COUNT and kb >= 8:
         s = max(1, min(math.ceil(SM_COUNT / tiles), kb // 4, 64))
         s = math.ceil(kb / math.ceil(kb / s))  # no empty split
-    Kp = _kpad(K)
-    part_off = 2 * batch * M * Kp * 4 + 2 * batch * N * Kp * 4 + 256
+    part_off = split_bytes(batch, M, K, N, fs) + 256
     return s, part_off
 
 
-def tail_plan(batch, M, K, N, bn, bk, splitk):
+def tail_plan(batch, M, K, N, bn, bk, splitk, fs=(False, False)):
     """The persistent GEMM's grid and last-wave split.
 
     Returns (grid, tail, cnt_off, tail_off, scratch_end): grid = min(SMs, tiles) CTAs; when the last
@@ -681,10 +691,36 @@ def tail_plan(batch, M, K, N, bn, bk, splitk):
         tail = min(grid // rem, (_kpad(K) // bk) // 4, 8)
     if tail < 2:
         return grid, 1, 0, 0, 0
-    Kp = _kpad(K)
-    cnt_off = 2 * batch * M * Kp * 4 + 2 * batch * N * Kp * 4 + 256
+    cnt_off = split_bytes(batch, M, K, N, fs) + 256
     tail_off = cnt_off + (4 * rem * 4 + 255) // 256 * 256
     return grid, tail, cnt_off, tail_off, tail_off + rem * tail * GEMM_BM * bn * 4
+
+
+FS_MAX_REREAD = 4   # split an operand inside the GEMM when at most this many output tiles load each of its tiles
+
+
+def fused_split_plan(batch, M, K, N, bn, a_t=False, b_t=False):
+    """(fa, fb): which operands the GEMM splits itself (TCB_FS_A / TCB_FS_B) instead of a split pass.
+
+    An operand qualifies when a TMA copy can read it raw (its row stride a multiple of 16 bytes) and it
+    is loaded by few output tiles: A by ceil(N / bn) of them, B by ceil(M / 128).  The in-kernel split
+    saves the split pass's write and re-read of hi and lo but repeats the conversion (in shared memory)
+    for every tile that loads the operand, so an operand shared by many tiles keeps its split pass.
+    TCB_GEMM_FUSED overrides: "0" neither, "1" both, "a" / "b" that operand only (when it qualifies)."""
+    import os
+    ea = M % 4 == 0 if a_t else K % 4 == 0
+    eb = K % 4 == 0 if b_t else N % 4 == 0
+    mode = os.environ.get("TCB_GEMM_FUSED")
+    if mode == "0":
+        return False, False
+    if mode == "1":
+        return ea, eb
+    if mode == "a":
+        return ea, False
+    if mode == "b":
+        return False, eb
+    most = int(os.environ.get("TCB_GEMM_FS_REREAD", FS_MAX_REREAD))
+    return ea and math.ceil(N / bn) <= most, eb and math.ceil(M / GEMM_BM) <= most
 
 
 def gemm_bn(N):
@@ -704,31 +740,52 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
     if batch > 65535 or math.ceil(M / GEMM_BM) > 65535:
         raise ValueError("matmul grid too large")
     Kp = _kpad(K)
-    a_bytes = batch * M * Kp * 4
-    b_bytes = batch * N * Kp * 4
-    err_off = 2 * a_bytes + 2 * b_bytes
-    splitk, part_off = splitk_plan(batch, M, K, N, bn)
+    fs = fused_split_plan(batch, M, K, N, bn, a_t, b_t)
+    err_off = split_bytes(batch, M, K, N, fs)
+    splitk, part_off = splitk_plan(batch, M, K, N, bn, fs)
     bk = gemm_bk(bn)
-    grid, tail, _, _, tail_end = tail_plan(batch, M, K, N, bn, bk, splitk)
+    grid, tail, _, _, tail_end = tail_plan(batch, M, K, N, bn, bk, splitk, fs)
     scratch = max(err_off + 256 + (splitk * batch * M * N * 4 if splitk > 1 else 0), tail_end)
-
-    maps = [("scratch", 0, Kp, M, batch, Kp * 4, M * Kp * 4, bk, GEMM_BM),
-            ("scratch", a_bytes, Kp, M, batch, Kp * 4, M * Kp * 4, bk, GEMM_BM),
-            ("scratch", 2 * a_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn),
-            ("scratch", 2 * a_bytes + b_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn)]
-    calls = [KernelCall("tcb_split_a", (Kp // 32, math.ceil(M / 32), batch) if a_t
-                        else grid1d(batch * M * Kp, per_thread=4), (256, 1, 1)),
-             KernelCall("tcb_split_b", grid1d(batch * N * Kp, per_thread=4) if b_t
-                        else (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)),
-             KernelCall("tcb_gemm_tc", (grid, 1, 1), (192, 1, 1), gemm_smem(bn, bk), [])]
-    calls[0].err_offset = err_off
-    calls[2].tma = maps
-    calls[2].err_offset = err_off
+    gemm = KernelCall("tcb_gemm_tc", (grid, 1, 1), (320 if any(fs) else 192, 1, 1), gemm_smem(bn, bk), [])
+    gemm.err_offset = err_off
+    a_bytes = 0 if fs[0] else batch * M * Kp * 4
+    b_off = 2 * a_bytes
+    b_bytes = batch * N * Kp * 4
+    ia, ib = (int(body.nodes[i].attrs["name"][1:]) for i in root.inputs)
+    # tensor maps [A_hi or raw A, A_lo, B_hi or raw B, B_lo]: split operands from scratch, raw ones from
+    # the launch operand in K-major {K, rows} boxes or MN-major {32, bk} boxes (a raw operand's second
+    # slot repeats its map and is not read)
+    if fs[0]:
+        ra = (("in", ia, M, K, batch, M * 4, K * M * 4, 32 | TMA_ATOM32, bk) if a_t else
+              ("in", ia, K, M, batch, K * 4, M * K * 4, bk, GEMM_BM))
+        maps = [ra, ra]
+    else:
+        maps = [("scratch", 0, Kp, M, batch, Kp * 4, M * Kp * 4, bk, GEMM_BM),
+                ("scratch", a_bytes, Kp, M, batch, Kp * 4, M * Kp * 4, bk, GEMM_BM)]
+    if fs[1]:
+        rb = (("in", ib, K, N, batch, K * 4, N * K * 4, bk, bn) if b_t else
+              ("in", ib, N, K, batch, N * 4, K * N * 4, 32 | TMA_ATOM32, bk))
+        maps += [rb, rb]
+    else:
+        maps += [("scratch", b_off, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn),
+                 ("scratch", b_off + b_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn)]
+    gemm.tma = maps
+    if fs[0]:
+        first = KernelCall("tcb_gemm_prep", (1, 1, 1), (128, 1, 1))
+    else:
+        first = KernelCall("tcb_split_a", (Kp // 32, math.ceil(M / 32), batch) if a_t
+                           else grid1d(batch * M * Kp, per_thread=4), (256, 1, 1))
+    first.err_offset = err_off
+    calls = [first]
+    if not fs[1]:
+        calls.append(KernelCall("tcb_split_b", grid1d(batch * N * Kp, per_thread=4) if b_t
+                                else (Kp // 32, math.ceil(N / 32), batch), (256, 1, 1)))
+    calls.append(gemm)
     if splitk > 1:
         calls.append(KernelCall("tcb_splitk_finish", grid1d(batch * M * N, per_thread=1), (256, 1, 1)))
     lau = Launch(node_id, op, kind, pattern, inputs, code, calls, scratch_bytes=scratch,
                  info={"mnk": (batch, M, K, N), "bn": bn, "bk": bk, "stages": gemm_stages(bn, bk), "splitk": splitk,
-                       "tail_split": tail, "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t})
+                       "tail_split": tail, "fused_split": fs, "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t})
     return lau
 
 
@@ -761,7 +818,8 @@ class KernelCall:
     """One kernel launch of a Launch: entry name, grid, block, dynamic smem, p[] parameters.
 
     ``tma``: tensor maps to build at launch, each (region, offset, cols, rows, batches, row_stride_bytes,
-    batch_stride_bytes, box_cols, box_rows) with region 'scratch'; ``err_offset``: where in scratch the
+    batch_stride_bytes, box_cols, box_rows) with region 'scratch' (offset = bytes into scratch) or 'in'
+    (offset = the launch operand's index); ``err_offset``: where in scratch the
     kernel's error word lives (its address goes in p[15]).
     """
     __slots__ = ("name", "grid", "block", "smem", "params", "tma", "err_offset")

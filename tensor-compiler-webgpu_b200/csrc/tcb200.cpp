@@ -356,7 +356,10 @@ int encode_maps(int n_maps, const uint64_t* d, TmaBlock* blk) {
   if (n_maps < 0 || n_maps > 4) return fail(TC_ERR_INVALID, "%d tensor maps (at most 4)", n_maps);
   for (int m = 0; m < n_maps; m++) {
     const uint64_t* v = d + 8 * m;
-    uint64_t addr = v[0], cols = v[1], rows = v[2], batches = v[3], rs = v[4], bs = v[5], bc = v[6], br = v[7];
+    uint64_t addr = v[0], cols = v[1], rows = v[2], batches = v[3], rs = v[4], bs = v[5], bc = v[6] & 0xFFFFFFFFull,
+             br = v[7];
+    const bool atom32 = (v[6] >> 32) & 1;  // 128-byte swizzle of 32-byte chunks (MN-major tf32 tiles)
+    if (atom32 && bc * 4 != 128) return fail(TC_ERR_INVALID, "tensor map %d: 32-byte-atom swizzle needs 128-byte rows", m);
     if (addr % 16) return fail(TC_ERR_INVALID, "tensor map %d: address not 16-byte aligned", m);
     if (rs % 16 || bs % 16) return fail(TC_ERR_INVALID, "tensor map %d: strides must be multiples of 16 bytes", m);
     if ((bc * 4 != 128 && bc * 4 != 64 && bc * 4 != 32) || br == 0 || br > 256)
@@ -368,7 +371,8 @@ int encode_maps(int n_maps, const uint64_t* d, TmaBlock* blk) {
     cuuint32_t box[3] = {(cuuint32_t)bc, (cuuint32_t)br, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     // the swizzle spans one box row: 128, 64 or 32 bytes
-    CUtensorMapSwizzle sw = bc * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+    CUtensorMapSwizzle sw = atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                            : bc * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                             : bc * 4 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
     CUresult r = CU(cuTensorMapEncodeTiled)(&blk->maps[m], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)addr, dims, strides,
                                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,

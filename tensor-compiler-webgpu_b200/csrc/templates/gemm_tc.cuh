@@ -90,9 +90,24 @@ __device__ __forceinline__ u64 sw128_desc(u32 saddr) {
   return d;
 }
 
-// Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = n.
-__host__ __device__ constexpr u32 idesc_tf32(u32 n) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((n >> 3) << 17) | ((u32)(GB_M >> 4) << 24);
+// MN-major tf32 operand tile (the M or N index contiguous): rows of 32 floats (128 bytes) along M/N,
+// one row per K index, in the 128-byte swizzle of 32-byte chunks (period 4 rows: the only MN-major
+// shared-memory layout the tensor cores take for 32-bit operands); 4-row groups 512 bytes apart, and
+// one such column of rows per 32 M (or N) indices, `lbo` bytes apart.
+__device__ __forceinline__ u64 mn_desc(u32 saddr, u32 lbo) {
+  u64 d = 0;
+  d |= (u64)((saddr >> 4) & 0x3FFF);                    // start address
+  d |= (u64)((lbo >> 4) & 0x3FFF) << 16;                 // leading byte offset: next 32 M/N indices
+  d |= (u64)(512 >> 4) << 32;                            // stride byte offset: next 4 K rows
+  d |= (u64)1 << 46;                                     // descriptor version for sm_100
+  d |= (u64)1 << 61;                                     // 128-byte swizzle, 32-byte atoms
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, M = 128, N = n; a_mn / b_mn: that operand is MN-major.
+__host__ __device__ constexpr u32 idesc_tf32(u32 n, u32 a_mn = 0, u32 b_mn = 0) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (a_mn << 15) | (b_mn << 16) | ((n >> 3) << 17) |
+         ((u32)(GB_M >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_tf32(u32 tmem, u64 a, u64 b, u32 idesc, u32 accumulate) {
@@ -117,6 +132,15 @@ __device__ __forceinline__ void tmem_ld16(u32 taddr, float (&r)[16]) {
   for (int j = 0; j < 16; ++j) r[j] = __uint_as_float(v[j]);
 }
 
+// The low part of x for the in-kernel split: the tensor core reads an fp32 operand as tf32 by
+// dropping its 13 low mantissa bits, so the raw value serves as hi and lo = rna_tf32(x - trunc(x)).
+__device__ __forceinline__ float tf32_lo(float x) {
+  const float t = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  u32 r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(__fsub_rn(x, t)));
+  return __uint_as_float(r);
+}
+
 __device__ __forceinline__ float tf32_rna(float x) {
   u32 r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -137,6 +161,15 @@ __device__ __forceinline__ float tf32_rna(float x) {
 #endif
 #ifndef TCB_PART_OFFSET
 #define TCB_PART_OFFSET 0ull
+#endif
+#ifndef TCB_FS_A
+#define TCB_FS_A 0   // 1: the GEMM reads raw A and makes its lo in shared memory (no split pass for A)
+#endif
+#ifndef TCB_FS_B
+#define TCB_FS_B 0   // the same for B
+#endif
+#ifndef TCB_SPLIT_B_OFFSET  // where split_b's B_hi, B_lo start in scratch (after A_hi, A_lo when A is split)
+#define TCB_SPLIT_B_OFFSET (2ull * TCB_BATCH * TCB_M * TCB_KP * 4)
 #endif
 #ifndef TCB_GRID
 #define TCB_GRID 148
@@ -240,7 +273,7 @@ extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a)
 
 // B [batch, K, N] -> B_hi^T, B_lo^T [batch, N, Kp] so both operands are K-major.
 extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a) {
-  float* hi = reinterpret_cast<float*>(a.scratch) + 2ull * TCB_BATCH * TCB_M * TCB_KP;
+  float* hi = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(a.scratch) + TCB_SPLIT_B_OFFSET);
   float* lo = hi + (u64)TCB_BATCH * TCB_N * TCB_KP;
   const float* src = reinterpret_cast<const float*>(a.in[TCB_IB]);
 #if TCB_B_T
@@ -250,12 +283,27 @@ extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a)
 #endif
 }
 
+// With A split in the kernel there is no tcb_split_a: this one-block launch, first in the tensor-core
+// launch, clears its error word (p[15]) and the tail units' arrival counters instead.
+extern "C" __global__ void __launch_bounds__(128) tcb_gemm_prep(const tcb::Args a) {
+  if (threadIdx.x == 0 && a.p[15]) *reinterpret_cast<u32*>(a.p[15]) = 0u;
+  u32* cnt = reinterpret_cast<u32*>(reinterpret_cast<unsigned char*>(a.scratch) + TCB_TAIL_CNT_OFFSET);
+  for (u32 i = threadIdx.x; i < 4 * tcb::GemmShape::REM; i += blockDim.x) cnt[i] = 0u;
+}
+
 // Persistent: TCB_GRID CTAs (one per SM) walk the work units (grouped raster for L2 reuse); TMEM holds
 // two BN-column accumulators so the epilogue of unit j overlaps the mainloop of unit j+1.
-extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_constant__ tcb::GemmParams P) {
+// An operand split in the kernel (TCB_FS_A / TCB_FS_B) arrives in the ring as its raw tile (K-major,
+// or MN-major when it arrives transposed: TCB_A_T for A, !TCB_B_T for B) and four more warps (6-9)
+// write the stage's lo tile beside it; the MMA reads the raw tile as hi.  An operand that is loaded by
+// many tiles keeps its split pass instead, so its conversion is not repeated per tile.
+extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192, 1)
+    tcb_gemm_tc(const __grid_constant__ tcb::GemmParams P) {
   using namespace tcb;
   using S = GemmShape;
   constexpr int BN = TCB_BN, STAGES = TCB_STAGES;
+  constexpr bool FA = TCB_FS_A != 0, FB = TCB_FS_B != 0, FS = FA || FB;
+  constexpr bool A_MN = FA && TCB_A_T, B_MN = FB && !TCB_B_T;
   constexpr u32 A_BYTES = GB_M * GB_K * 4, B_BYTES = BN * GB_K * 4;
   constexpr u32 STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   constexpr u32 KB_PER = (S::KB_ALL + TCB_SPLITK - 1) / TCB_SPLITK;  // k-blocks per split
@@ -270,14 +318,15 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
   const u32 raw = smem_u32(smem_raw);
   const u32 base = (raw + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
-  const u32 bars = base + STAGES * STAGE_BYTES;  // full[S], empty[S], accf[2], acce[2]
-  u32* tmem_slot = reinterpret_cast<u32*>(gbase + STAGES * STAGE_BYTES + (2 * STAGES + 4) * 8);
+  const u32 bars = base + STAGES * STAGE_BYTES;  // full[S], empty[S], accf[2], acce[2], conv[S]
+  u32* tmem_slot = reinterpret_cast<u32*>(gbase + STAGES * STAGE_BYTES + (3 * STAGES + 4) * 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto full = [&](int s) { return bars + 8u * s; };
   auto empty = [&](int s) { return bars + 8u * (STAGES + s); };
   auto accf = [&](u32 b) { return bars + 8u * (2 * STAGES + b); };
   auto acce = [&](u32 b) { return bars + 8u * (2 * STAGES + 2 + b); };
+  auto conv = [&](int s) { return bars + 8u * (2 * STAGES + 4 + s); };
   struct Tile { int m0, n0, bz; u32 kb0, kb; int tail; u32 piece; };
   auto decode = [&](u32 u) {
     Tile T;
@@ -312,6 +361,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(full(s), 1); mbar_init(empty(s), 1); }
     for (u32 b = 0; b < 2; ++b) { mbar_init(accf(b), 1); mbar_init(acce(b), 4); }
+    if (FS) for (int s = 0; s < STAGES; ++s) mbar_init(conv(s), 128);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -334,12 +384,26 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
           const int s = it % STAGES;
           if (it >= (u32)STAGES && !mbar_wait(empty(s), ((it / STAGES) - 1) & 1, err, 1)) { ok = false; break; }
           const u32 st = base + s * STAGE_BYTES;
-          mbar_expect_tx(full(s), STAGE_BYTES);
           const int kc = (int)((T.kb0 + kb) * GB_K);
-          tma_load_3d(st, &P.maps[0], full(s), kc, T.m0, T.bz);
-          tma_load_3d(st + A_BYTES, &P.maps[1], full(s), kc, T.m0, T.bz);
-          tma_load_3d(st + 2 * A_BYTES, &P.maps[2], full(s), kc, T.n0, T.bz);
-          tma_load_3d(st + 2 * A_BYTES + B_BYTES, &P.maps[3], full(s), kc, T.n0, T.bz);
+          // maps: [0] A_hi or raw A, [1] A_lo, [2] B_hi or raw B, [3] B_lo; an MN-major raw tile is GB_K
+          // rows of 32 floats per 32 M (N) indices (128-byte swizzle of 32-byte chunks)
+          mbar_expect_tx(full(s), (FA ? A_BYTES : 2 * A_BYTES) + (FB ? B_BYTES : 2 * B_BYTES));
+          if (A_MN) {
+#pragma unroll
+            for (int q = 0; q < GB_M / 32; ++q)
+              tma_load_3d(st + q * GB_K * 128, &P.maps[0], full(s), T.m0 + 32 * q, kc, T.bz);
+          } else {
+            tma_load_3d(st, &P.maps[0], full(s), kc, T.m0, T.bz);
+          }
+          if (!FA) tma_load_3d(st + A_BYTES, &P.maps[1], full(s), kc, T.m0, T.bz);
+          if (B_MN) {
+#pragma unroll
+            for (int q = 0; q < BN / 32; ++q)
+              tma_load_3d(st + 2 * A_BYTES + q * GB_K * 128, &P.maps[2], full(s), T.n0 + 32 * q, kc, T.bz);
+          } else {
+            tma_load_3d(st + 2 * A_BYTES, &P.maps[2], full(s), kc, T.n0, T.bz);
+          }
+          if (!FB) tma_load_3d(st + 2 * A_BYTES + B_BYTES, &P.maps[3], full(s), kc, T.n0, T.bz);
         }
       }
       // drain: wait (bounded) for the copies still in flight before this CTA may exit
@@ -347,7 +411,10 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr u32 ID = idesc_tf32(BN);
+      constexpr u32 ID = idesc_tf32(BN, A_MN ? 1u : 0u, B_MN ? 1u : 0u);
+      // operand descriptors of K step k (8 K indices) in a tile at `t`
+      auto da = [&](u32 t, int k) { return A_MN ? mn_desc(t + 1024 * k, GB_K * 128) : sw128_desc(t + 32 * k); };
+      auto db = [&](u32 t, int k) { return B_MN ? mn_desc(t + 1024 * k, GB_K * 128) : sw128_desc(t + 32 * k); };
       u32 it = 0, j = 0;
       bool ok = true;
       for (u32 t = blockIdx.x; ok && t < S::UNITS; t += S::GRID, ++j) {
@@ -359,12 +426,13 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
         for (u32 kb = 0; kb < T.kb; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(full(s), (it / STAGES) & 1, err, 3)) { ok = false; break; }
+          if (FS && !mbar_wait(conv(s), (it / STAGES) & 1, err, 7)) { ok = false; break; }
           tc_fence_after();
           const u32 st = base + s * STAGE_BYTES;
 #pragma unroll
           for (int k = 0; k < GB_K / 8; ++k) {
-            const u64 ah = sw128_desc(st + 32 * k), al = sw128_desc(st + A_BYTES + 32 * k);
-            const u64 bh = sw128_desc(st + 2 * A_BYTES + 32 * k), bl = sw128_desc(st + 2 * A_BYTES + B_BYTES + 32 * k);
+            const u64 ah = da(st, k), al = da(st + A_BYTES, k);
+            const u64 bh = db(st + 2 * A_BYTES, k), bl = db(st + 2 * A_BYTES + B_BYTES, k);
             mma_tf32(acc, al, bh, ID, (kb | k) != 0);
             mma_tf32(acc, ah, bl, ID, 1);
             mma_tf32(acc, ah, bh, ID, 1);
@@ -372,6 +440,40 @@ extern "C" __global__ void __launch_bounds__(192, 1) tcb_gemm_tc(const __grid_co
           mma_commit(empty(s));
         }
         mma_commit(accf(buf));  // with no k-block in this split the accumulator is never enabled: see the epilogue
+      }
+    }
+  } else if (FS && warp >= 6) {
+    // in-kernel split: lo of every raw value of the stage, written beside it (same swizzled position)
+    const int tid = threadIdx.x - 192;
+    u32 it = 0;
+    bool ok = true;
+    for (u32 t = blockIdx.x; ok && t < S::UNITS; t += S::GRID) {
+      const Tile T = decode(t);
+      for (u32 kb = 0; kb < T.kb; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(full(s), (it / STAGES) & 1, err, 6)) { ok = false; break; }
+        unsigned char* st = gbase + s * STAGE_BYTES;
+        if (FA) {
+          const float4* ra = reinterpret_cast<const float4*>(st);
+          float4* la = reinterpret_cast<float4*>(st + A_BYTES);
+#pragma unroll
+          for (u32 v = tid; v < A_BYTES / 16; v += 128) {
+            const float4 x = ra[v];
+            la[v] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+          }
+        }
+        if (FB) {
+          const float4* rb = reinterpret_cast<const float4*>(st + 2 * A_BYTES);
+          float4* lb = reinterpret_cast<float4*>(st + 2 * A_BYTES + B_BYTES);
+#pragma unroll
+          for (u32 v = tid; v < B_BYTES / 16; v += 128) {
+            const float4 x = rb[v];
+            lb[v] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+          }
+        }
+        // make these generic-proxy writes visible to the tensor core, then release the stage to the MMA
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(conv(s)) : "memory");
       }
     }
   } else {

@@ -212,13 +212,20 @@ class Module:
         self.runner = runner
 
 
-def _map_desc(call, scratch):
-    """The 8-value tensor-map descriptors of a call (include/tcb200.h, tc_launch_tma)."""
+def _map_desc(call, scratch, ins=()):
+    """The 8-value tensor-map descriptors of a call (include/tcb200.h, tc_launch_tma): each map is over
+    scratch (at an offset) or over one of the launch's operands ('in', operand index)."""
     vals = []
     for region, off, cols, rows, batches, rs, bs, bc, br in call.tma:
-        if region != "scratch":
+        if region == "scratch":
+            addr = scratch + off
+        elif region == "in":
+            addr = ins[off]
+        else:
             raise ValueError(f"tensor map over '{region}'")
-        vals += [scratch + off, cols, rows, batches, rs, bs, bc, br]
+        if addr % 16:
+            raise ValueError(f"{call.name}: tensor map base {addr:#x} is not 16-byte aligned")
+        vals += [addr, cols, rows, batches, rs, bs, bc, br]
     return (ctypes.c_uint64 * len(vals))(*vals)
 
 
@@ -236,7 +243,7 @@ def issue(call, mod, ins, out, scratch, plan=None, err_ptr=None):
     args = make_args(ins, out, scratch, params)
     g, b = _u32x3(call.grid), _u32x3(call.block)
     if call.tma:
-        desc = _map_desc(call, scratch)
+        desc = _map_desc(call, scratch, ins)
         if plan is None:
             check(lib().tc_launch_tma(mod.handle, call.name.encode(), g, b, call.smem, len(call.tma), desc,
                                       ctypes.byref(args)))

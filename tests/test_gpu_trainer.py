@@ -45,7 +45,14 @@ def test_fused_trainer_matches_checked_path_bitwise(pkg, runner):
         tr.destroy()
 
 
-def test_dp_trainer_world1_matches_fused_step(pkg, runner):
+@pytest.mark.parametrize("split_mode,rtol,atol", [("0", 1e-4, 1e-6), (None, 1e-3, 1e-5)])
+def test_dp_trainer_world1_matches_fused_step(pkg, runner, monkeypatch, split_mode, rtol, atol):
+    """The data-parallel trainer at world size 1 against the fused step.  With every GEMM operand split
+    by a split pass ("0") both compute the same products; by default the folded program may split an
+    operand inside the GEMM where the unfolded one cannot (hi = trunc(x) there, rna(x) in the pass), so
+    the parameters after three Adam steps agree to the looser tolerance."""
+    if split_mode is not None:
+        monkeypatch.setenv("TCB_GEMM_FUSED", split_mode)
     rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
     wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
     dp = importlib.import_module("tensor-compiler-webgpu_b200.dp")
@@ -66,15 +73,19 @@ def test_dp_trainer_world1_matches_fused_step(pkg, runner):
         pa = ref.read(tr.names)
         pb = tr.read(tr.names)
         for k in tr.names:
-            np.testing.assert_allclose(pb[k], pa[k], rtol=1e-4, atol=1e-6, err_msg=k)
+            np.testing.assert_allclose(pb[k], pa[k], rtol=rtol, atol=atol, err_msg=k)
     finally:
         ref.destroy()
         tr.destroy()
 
 
-def test_folded_transposes_and_aliased_reshapes_change_no_bit(pkg, runner):
+def test_folded_transposes_and_aliased_reshapes_change_no_bit(pkg, runner, monkeypatch):
     """The resident program (transposes folded into GEMM operand splits, reshapes aliased) gives the
-    verification path's values bit for bit on the loss and every gradient."""
+    verification path's values bit for bit on the loss and every gradient, with every GEMM operand
+    split by a split pass.  (A fold can change whether an operand qualifies for the in-kernel split --
+    its raw row stride is K or M -- and that split takes hi = trunc(x) instead of rna(x): same budget,
+    other bits.)"""
+    monkeypatch.setenv("TCB_GEMM_FUSED", "0")
     rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
     cg = importlib.import_module("tensor-compiler-webgpu_b200.codegen")
     wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
