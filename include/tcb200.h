@@ -102,10 +102,10 @@ int tc_module_free(tc_module* mod);
 /* One dispatch (runtime.js:86-101's setPipeline/setBindGroup/dispatchWorkgroups). */
 int tc_launch(tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],
               uint32_t smem_bytes, const tc_args* args);
-/* A dispatch of a TMA-fed kernel: up to 4 fp32 tensor maps (zero fill out
+/* A dispatch of a TMA-fed kernel: up to 5 fp32 tensor maps (zero fill out
  * of bounds) are built from 8 values each -- (address, cols, rows, batches,
  * row_stride_bytes, batch_stride_bytes, box_cols, box_rows) -- and passed,
- * 64-byte aligned, before the tc_args block.  The address must be 16-byte
+ * 64-byte aligned, in five map slots before the tc_args block.  The address must be 16-byte
  * aligned, the strides multiples of 16 bytes, box_cols * 4 one of 128, 64 or
  * 32 bytes (the swizzle width: 128B, 64B or 32B), box_rows at most 256.
  * Bit 32 of box_cols (with 32 floats in its low bits) asks for the 128-byte

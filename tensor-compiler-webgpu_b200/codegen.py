@@ -591,6 +591,7 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=Fa
         grid, tail, cnt_off, tail_off, _ = tail_plan(batch, M, K, N, bn, bk, splitk, fs)
         tc_defs = (f"#define TCB_KP {_kpad(K)}\n#define TCB_BN {bn}\n#define TCB_BK {bk}\n"
                    f"#define TCB_FS_A {int(fs[0])}\n#define TCB_FS_B {int(fs[1])}\n"
+                   f"#define TCB_TMA_STORE {int(tma_store_ok(N, splitk))}\n"
                    f"#define TCB_SPLIT_B_OFFSET {0 if fs[0] else 2 * batch * M * _kpad(K) * 4}ull\n"
                    f"#define TCB_STAGES {gemm_stages(bn, bk)}\n"
                    f"#define TCB_SPLITK {splitk}\n#define TCB_PART_OFFSET {part_off}ull\n"
@@ -633,13 +634,22 @@ def gemm_stage_bytes(bn, bk):
     return 2 * GEMM_BM * bk * 4 + 2 * bn * bk * 4
 
 
+GEMM_STAGING = 4 * 2 * 32 * 32 * 4   # output staging: two 32 x 32 float blocks per epilogue warp
+
+
 def gemm_stages(bn, bk=32):
-    return max(2, min(6, (SMEM_LIMIT - 2048) // gemm_stage_bytes(bn, bk)))
+    return max(2, min(6, (SMEM_LIMIT - 2048 - GEMM_STAGING) // gemm_stage_bytes(bn, bk)))
 
 
 def gemm_smem(bn, bk=32):
-    st = gemm_stages(bn, bk)
-    return st * gemm_stage_bytes(bn, bk) + (3 * st + 4) * 8 + 16 + 1024
+    """Ring + 1 KB of barriers + output staging + 1 KB to align the ring to 1024 bytes."""
+    return gemm_stages(bn, bk) * gemm_stage_bytes(bn, bk) + 1024 + GEMM_STAGING + 1024
+
+
+def tma_store_ok(N, splitk):
+    """The epilogue writes through TMA stores when the output's row stride is a multiple of 16 bytes
+    (split-K launches write partial sums instead)."""
+    return N % 4 == 0 and splitk == 1
 
 
 def gemm_bk(bn=128):
@@ -769,6 +779,8 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
     else:
         maps += [("scratch", b_off, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn),
                  ("scratch", b_off + b_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn)]
+    if tma_store_ok(N, splitk):
+        maps.append(("out", 0, N, M, batch, N * 4, M * N * 4, 32, 32))
     gemm.tma = maps
     if fs[0]:
         first = KernelCall("tcb_gemm_prep", (1, 1, 1), (128, 1, 1))
@@ -818,8 +830,8 @@ class KernelCall:
     """One kernel launch of a Launch: entry name, grid, block, dynamic smem, p[] parameters.
 
     ``tma``: tensor maps to build at launch, each (region, offset, cols, rows, batches, row_stride_bytes,
-    batch_stride_bytes, box_cols, box_rows) with region 'scratch' (offset = bytes into scratch) or 'in'
-    (offset = the launch operand's index); ``err_offset``: where in scratch the
+    batch_stride_bytes, box_cols, box_rows) with region 'scratch' (offset = bytes into scratch), 'in'
+    (offset = the launch operand's index) or 'out'; ``err_offset``: where in scratch the
     kernel's error word lives (its address goes in p[15]).
     """
     __slots__ = ("name", "grid", "block", "smem", "params", "tma", "err_offset")

@@ -321,7 +321,7 @@ int tc_host_free(void* p) {
 namespace {
 
 struct TmaBlock {
-  alignas(64) CUtensorMap maps[4];
+  alignas(64) CUtensorMap maps[5];
   tc_args args;
 };
 
@@ -353,7 +353,7 @@ int prepare_smem(CUfunction fn, uint32_t smem) {
 }
 
 int encode_maps(int n_maps, const uint64_t* d, TmaBlock* blk) {
-  if (n_maps < 0 || n_maps > 4) return fail(TC_ERR_INVALID, "%d tensor maps (at most 4)", n_maps);
+  if (n_maps < 0 || n_maps > 5) return fail(TC_ERR_INVALID, "%d tensor maps (at most 5)", n_maps);
   for (int m = 0; m < n_maps; m++) {
     const uint64_t* v = d + 8 * m;
     uint64_t addr = v[0], cols = v[1], rows = v[2], batches = v[3], rs = v[4], bs = v[5], bc = v[6] & 0xFFFFFFFFull,

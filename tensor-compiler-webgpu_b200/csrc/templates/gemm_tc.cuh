@@ -29,7 +29,7 @@ namespace tcb {
 
 struct alignas(64) TmaDesc { u64 v[16]; };
 struct GemmParams {
-  TmaDesc maps[4];  // A_hi, A_lo, B_hi, B_lo (3-D: {Kp, rows, batch})
+  TmaDesc maps[5];  // A_hi / raw A, A_lo, B_hi / raw B, B_lo (3-D: {cols, rows, batch}); [4] the output
   Args a;
 };
 
@@ -71,6 +71,17 @@ __device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity, u32* err, u32 cod
     }
   }
 }
+
+// Shared -> global tensor store of one box (rows outside the tensor are not written); completion is
+// tracked per thread in bulk groups.
+__device__ __forceinline__ void tma_store_3d(const TmaDesc* map, u32 src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               :: "l"(reinterpret_cast<u64>(map)), "r"(src), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most one committed group still has to read its shared-memory source
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_3d(u32 dst, const TmaDesc* map, u32 bar, int c0, int c1, int c2) {
   asm volatile(
@@ -170,6 +181,9 @@ __device__ __forceinline__ float tf32_rna(float x) {
 #endif
 #ifndef TCB_SPLIT_B_OFFSET  // where split_b's B_hi, B_lo start in scratch (after A_hi, A_lo when A is split)
 #define TCB_SPLIT_B_OFFSET (2ull * TCB_BATCH * TCB_M * TCB_KP * 4)
+#endif
+#ifndef TCB_TMA_STORE
+#define TCB_TMA_STORE 0   // 1: the epilogue stages 32 x 32 output blocks in shared memory for TMA stores (map 4)
 #endif
 #ifndef TCB_GRID
 #define TCB_GRID 148
@@ -319,6 +333,9 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
   const u32 base = (raw + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
   const u32 bars = base + STAGES * STAGE_BYTES;  // full[S], empty[S], accf[2], acce[2], conv[S]
+  // output staging (TCB_TMA_STORE): two 32 x 32 float blocks per epilogue warp, after a 1 KB barrier area
+  const u32 staging = bars + 1024;
+  static_assert((3 * STAGES + 4) * 8 + 16 <= 1024, "barrier area");
   u32* tmem_slot = reinterpret_cast<u32*>(gbase + STAGES * STAGE_BYTES + (3 * STAGES + 4) * 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -499,7 +516,7 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
         for (int jj = 0; jj < 16; ++jj) if ((u64)(T.n0 + c0 + jj) < (u64)TCB_N) out[base_i + jj] = o[jj];
       }
     };
-    u32 j = 0;
+    u32 j = 0, nstore = 0;
     for (u32 t = blockIdx.x; t < S::UNITS; t += S::GRID, ++j) {
       const Tile T = decode(t);
       const u32 buf = j & 1;
@@ -553,7 +570,47 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
             }
             finish16(T, row, c0, v);
           }
+          // every piece has arrived: leave the counter at zero for the next launch
+          if (lane == 0) reinterpret_cast<u32*>(scr + TCB_TAIL_CNT_OFFSET)[4 * (u32)T.tail + (u32)q] = 0u;
         }
+        continue;
+      }
+      if (TCB_TMA_STORE && TCB_SPLITK == 1) {
+        // 32 columns at a time: the fused body on this row's 32 values, written into a 128-byte-swizzled
+        // 32 x 32 staging block (conflict-free: 16-byte chunk c of row r at r * 128 + (c ^ (r & 7)) * 16),
+        // then one TMA store of the block; two blocks per warp alternate.
+        const int r = 32 * q + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32, ++nstore) {
+          float v[32];
+          tmem_ld16(tmem + buf * BN + ((u32)(32 * q) << 16) + (u32)c0, *reinterpret_cast<float(*)[16]>(&v[0]));
+          tmem_ld16(tmem + buf * BN + ((u32)(32 * q) << 16) + (u32)(c0 + 16), *reinterpret_cast<float(*)[16]>(&v[16]));
+          const u64 grow = (u64)T.m0 + r;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const u64 col = (u64)(T.n0 + c0 + jj);
+            const float acc = T.kb == 0 ? 0.0f : v[jj];
+            v[jj] = (grow < (u64)TCB_M && col < (u64)TCB_N)
+                        ? Epi::apply(P.a, acc, (u64)T.bz * TCB_M * TCB_N + grow * TCB_N + col, grow, col, (u64)T.bz)
+                        : 0.0f;
+          }
+          const u32 blk = staging + (u32)((q * 2 + (nstore & 1)) * 4096);
+          if (lane == 0 && nstore >= 2) bulk_wait_read1();
+          __syncwarp();
+          float4* sp = reinterpret_cast<float4*>(gbase + (blk - base));
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            sp[lane * 8 + (c ^ (lane & 7))] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&P.maps[4], blk, T.n0 + c0, T.m0 + 32 * q, T.bz);
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(acce(buf)) : "memory");
         continue;
       }
 #pragma unroll 1
@@ -582,6 +639,7 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(acce(buf)) : "memory");
     }
+    if (TCB_TMA_STORE && lane == 0) bulk_wait_all();  // the staged stores are done before the CTA exits
   }
   tc_fence_before();
   __syncthreads();

@@ -212,15 +212,17 @@ class Module:
         self.runner = runner
 
 
-def _map_desc(call, scratch, ins=()):
+def _map_desc(call, scratch, ins=(), out=0):
     """The 8-value tensor-map descriptors of a call (include/tcb200.h, tc_launch_tma): each map is over
-    scratch (at an offset) or over one of the launch's operands ('in', operand index)."""
+    scratch (at an offset), one of the launch's operands ('in', operand index) or its output ('out')."""
     vals = []
     for region, off, cols, rows, batches, rs, bs, bc, br in call.tma:
         if region == "scratch":
             addr = scratch + off
         elif region == "in":
             addr = ins[off]
+        elif region == "out":
+            addr = out + off
         else:
             raise ValueError(f"tensor map over '{region}'")
         if addr % 16:
@@ -243,7 +245,7 @@ def issue(call, mod, ins, out, scratch, plan=None, err_ptr=None):
     args = make_args(ins, out, scratch, params)
     g, b = _u32x3(call.grid), _u32x3(call.block)
     if call.tma:
-        desc = _map_desc(call, scratch, ins)
+        desc = _map_desc(call, scratch, ins, out)
         if plan is None:
             check(lib().tc_launch_tma(mod.handle, call.name.encode(), g, b, call.smem, len(call.tma), desc,
                                       ctypes.byref(args)))
