@@ -227,7 +227,7 @@ def run_ours(args):
         prog.write(nid, inputs[name])
     # the dominant kernel: the launch moving the most algorithmic bytes (C3: the tensor-core GEMM kernel)
     dom = max(range(len(launches)), key=lambda k: launches[k].bytes)
-    flat = [(k, c) for k, lau in enumerate(launches) for c in lau.calls]
+    flat = [(k, c) for k, lau in enumerate(launches) for c in rt.program_calls(lau)]
     tensor = args.workload == "c3"
     if tensor:
         dcall = next(i for i, (k, c) in enumerate(flat) if c.name in ("tcb_gemm_tc", "tcb_matmul"))
@@ -239,7 +239,7 @@ def run_ours(args):
     seg = rt.Segments(prog, [dcall, dcall + 1])
     K, Wm = args.steps, args.warmup
     ev = rt.Events(runner, 2 * K + 2)
-    kernel_calls = sum(len(l.calls) for l in launches)
+    kernel_calls = prog.kernel_launches
 
     def step(k=None):
         seg.run(0)

@@ -588,7 +588,7 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=Fa
         fs = fused_split_plan(batch, M, K, N, bn, a_t, b_t)
         splitk, part_off = splitk_plan(batch, M, K, N, bn, fs)
         bk = gemm_bk(bn)
-        grid, tail, cnt_off, tail_off, _ = tail_plan(batch, M, K, N, bn, bk, splitk, fs)
+        grid, tail, _, tail_off, _ = tail_plan(batch, M, K, N, bn, bk, splitk, fs)
         tc_defs = (f"#define TCB_KP {_kpad(K)}\n#define TCB_BN {bn}\n#define TCB_BK {bk}\n"
                    f"#define TCB_FS_A {int(fs[0])}\n#define TCB_FS_B {int(fs[1])}\n"
                    f"#define TCB_TMA_STORE {int(tma_store_ok(N, splitk))}\n"
@@ -596,7 +596,7 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=Fa
                    f"#define TCB_STAGES {gemm_stages(bn, bk)}\n"
                    f"#define TCB_SPLITK {splitk}\n#define TCB_PART_OFFSET {part_off}ull\n"
                    f"#define TCB_GRID {grid}\n#define TCB_TAIL_SPLIT {tail}\n"
-                   f"#define TCB_TAIL_CNT_OFFSET {cnt_off}ull\n#define TCB_TAIL_OFFSET {tail_off}ull\n"
+                   f"#define TCB_TAIL_OFFSET {tail_off}ull\n"
                    f"#define TCB_A_T {int(a_t)}\n#define TCB_B_T {int(b_t)}\n")
     src = f"""// matmul epilogue ({kernel}): batch {batch}, [{M},{K}] x [{K},{N}]
 #include "tcb/common.cuh"
@@ -677,33 +677,47 @@ def splitk_plan(batch, M, K, N, bn, fs=(False, False)):
     tiles = batch * math.ceil(M / GEMM_BM) * math.ceil(N / bn)
     kb = _kpad(K) // 32
     s = 1
-    if tiles < SM_COUNT and kb >= 8:
-        s = max(1, min(math.ceil(SM_COUNT / tiles), kb // 4, 64))
+    # up to 8 K ranges per tile are reduced inside the GEMM by the last arriver (tail_plan); split-K
+    # with a finishing pass only when the SMs need more than that (tiles <= SMs / 9)
+    if tiles < SM_COUNT and SM_COUNT // tiles > 8 and kb >= 8:
+        s = max(1, min(SM_COUNT // tiles, kb // 4, 64))
         s = math.ceil(kb / math.ceil(kb / s))  # no empty split
     part_off = split_bytes(batch, M, K, N, fs) + 256
     return s, part_off
 
 
-def tail_plan(batch, M, K, N, bn, bk, splitk, fs=(False, False)):
-    """The persistent GEMM's grid and last-wave split.
+def ctrl_bytes(rem):
+    """A tensor-core launch's control block: its error word (16 bytes) and 4 arrival counters per split
+    tile, 64-byte aligned."""
+    return (16 + 16 * rem + 63) // 64 * 64
 
-    Returns (grid, tail, cnt_off, tail_off, scratch_end): grid = min(SMs, tiles) CTAs; when the last
-    wave would hold rem <= grid/2 tiles, each of them is cut into `tail` K ranges (>= 4 k-blocks each,
-    at most 8) so that wave fills the SMs.  Their arrival counters (4 per tile) sit at cnt_off and
-    their partial tiles (128 x bn floats per range) at tail_off in scratch; scratch_end is the end of
-    that region (0 when there is no split).
+
+def tail_plan(batch, M, K, N, bn, bk, splitk, fs=(False, False)):
+    """The persistent GEMM's grid and K-range split of the tiles of its last wave.
+
+    Returns (grid, tail, rem, tail_off, scratch_end).  grid = min(SMs, tiles) CTAs; when the last wave
+    would hold rem <= grid/2 tiles, each of them is cut into `tail` K ranges (>= 4 k-blocks each, at
+    most 8) so that wave fills the SMs.  With fewer tiles than SMs that is every tile: grid becomes
+    tiles x tail, one range per CTA.  The ranges' partial tiles (128 x bn floats each) sit at tail_off
+    in scratch, after the control block; scratch_end is the end of that region (0 when nothing is split).
     """
     tiles = batch * math.ceil(M / GEMM_BM) * math.ceil(N / bn) * splitk
-    grid = min(SM_COUNT, tiles)
-    rem = tiles % grid
-    tail = 1
-    if splitk == 1 and rem and 2 * rem <= grid:
-        tail = min(grid // rem, (_kpad(K) // bk) // 4, 8)
-    if tail < 2:
-        return grid, 1, 0, 0, 0
-    cnt_off = split_bytes(batch, M, K, N, fs) + 256
-    tail_off = cnt_off + (4 * rem * 4 + 255) // 256 * 256
-    return grid, tail, cnt_off, tail_off, tail_off + rem * tail * GEMM_BM * bn * 4
+    kbs = _kpad(K) // bk
+    if splitk == 1 and tiles < SM_COUNT:
+        tail = min(SM_COUNT // tiles, kbs // 4, 8)
+        if tail < 2:
+            return tiles, 1, 0, 0, 0
+        grid, rem = tiles * tail, tiles
+    else:
+        grid = min(SM_COUNT, tiles)
+        rem = tiles % grid
+        tail = 1
+        if splitk == 1 and rem and 2 * rem <= grid:
+            tail = min(grid // rem, kbs // 4, 8)
+        if tail < 2:
+            return grid, 1, 0, 0, 0
+    tail_off = split_bytes(batch, M, K, N, fs) + max(256, (ctrl_bytes(rem) + 255) // 256 * 256)
+    return grid, tail, rem, tail_off, tail_off + rem * tail * GEMM_BM * bn * 4
 
 
 FS_MAX_REREAD = 4   # split an operand inside the GEMM when at most this many output tiles load each of its tiles
@@ -754,7 +768,7 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
     err_off = split_bytes(batch, M, K, N, fs)
     splitk, part_off = splitk_plan(batch, M, K, N, bn, fs)
     bk = gemm_bk(bn)
-    grid, tail, _, _, tail_end = tail_plan(batch, M, K, N, bn, bk, splitk, fs)
+    grid, tail, rem, _, tail_end = tail_plan(batch, M, K, N, bn, bk, splitk, fs)
     scratch = max(err_off + 256 + (splitk * batch * M * N * 4 if splitk > 1 else 0), tail_end)
     gemm = KernelCall("tcb_gemm_tc", (grid, 1, 1), (320 if any(fs) else 192, 1, 1), gemm_smem(bn, bk), [])
     gemm.err_offset = err_off
@@ -797,7 +811,8 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
         calls.append(KernelCall("tcb_splitk_finish", grid1d(batch * M * N, per_thread=1), (256, 1, 1)))
     lau = Launch(node_id, op, kind, pattern, inputs, code, calls, scratch_bytes=scratch,
                  info={"mnk": (batch, M, K, N), "bn": bn, "bk": bk, "stages": gemm_stages(bn, bk), "splitk": splitk,
-                       "tail_split": tail, "fused_split": fs, "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t})
+                       "tail_split": tail, "ctrl_bytes": ctrl_bytes(rem), "fused_split": fs,
+                       "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t})
     return lau
 
 
@@ -869,6 +884,28 @@ def grid1d(n, per_thread=4, block=WG, waves=8):
     return (max(1, min(math.ceil(chunks / block), SM_COUNT * waves)), 1, 1)
 
 
+def copy_source(w=4):
+    """An elementwise source that copies its operand (out[i] = in0[i]), `w` floats per step; the element
+    count comes from p[0], so one module serves copies of every size (a resident program's feedback)."""
+    return f"""// device copy, {w} floats per step
+#include "tcb/common.cuh"
+#define TCB_W {w}
+struct Body {{
+  template <int W> struct Regs {{
+    float x0[W];
+  }};
+  template <int W> __device__ __forceinline__ static void load(const tcb::Args& a, u64 i0, Regs<W>& r) {{
+    tcb::load<W>(r.x0, reinterpret_cast<const float*>(a.in[0]) + i0);
+  }}
+  template <int W> __device__ __forceinline__ static void compute(const Regs<W>& r, float (&o)[W]) {{
+#pragma unroll
+    for (int l = 0; l < W; ++l) o[l] = r.x0[l];
+  }}
+}};
+#include "tcb/elementwise.cuh"
+"""
+
+
 def _ew_launch(body, out_id, n, kind, node_id, op, pattern, inputs, sabotage=None, tag="elementwise"):
     code = _elementwise_source(body, out_id, n, tag=tag)
     count = n + 1 if sabotage == "fused-bounds-off-by-one" else n
@@ -917,7 +954,7 @@ def _reduce_launch(op, in_shape, axis, node_id, inputs):
         calls = [KernelCall("tcb_reduce_cols", (gx, split, 1), (256, 1, 1))]
         scratch = 0
         if split > 1:
-            calls.append(KernelCall("tcb_reduce_finish", (max(1, min(math.ceil(outs / 256), SM_COUNT * 8)), 1, 1),
+            calls.append(KernelCall("tcb_reduce_finish", (max(1, min(math.ceil(outs / 32), SM_COUNT * 8)), 1, 1),
                                     (256, 1, 1)))
             scratch = split * outs * 4
     return Launch(node_id, op, op, None, inputs, code, calls, scratch_bytes=scratch,

@@ -14,7 +14,8 @@
 #define TCB_UNROLL 2
 #endif
 
-extern "C" __global__ void __launch_bounds__(256) tcb_elementwise(const tcb::Args a) {
+namespace tcb {
+__device__ __forceinline__ void elementwise_run(const tcb::Args& a) {
   const u64 n = (u64)a.p[0];
   constexpr int W = TCB_W;
   constexpr int U = TCB_UNROLL;
@@ -50,4 +51,13 @@ extern "C" __global__ void __launch_bounds__(256) tcb_elementwise(const tcb::Arg
       out[i] = o[0];
     }
   }
+}
+}  // namespace tcb
+
+extern "C" __global__ void __launch_bounds__(256) tcb_elementwise(const tcb::Args a) { tcb::elementwise_run(a); }
+
+// Several launches of this same body over different buffers in one launch (a resident program batches
+// small independent ones): a.scratch holds a device table of argument blocks, blockIdx.y picks one.
+extern "C" __global__ void __launch_bounds__(256) tcb_elementwise_multi(const tcb::Args a) {
+  tcb::elementwise_run(reinterpret_cast<const tcb::Args*>(a.scratch)[blockIdx.y]);
 }

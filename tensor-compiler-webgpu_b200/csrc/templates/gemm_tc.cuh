@@ -194,9 +194,6 @@ __device__ __forceinline__ float tf32_rna(float x) {
 #ifndef TCB_TAIL_OFFSET
 #define TCB_TAIL_OFFSET 0ull
 #endif
-#ifndef TCB_TAIL_CNT_OFFSET
-#define TCB_TAIL_CNT_OFFSET 0ull
-#endif
 
 namespace tcb {
 // Work units of the persistent GEMM (TCB_GRID CTAs, unit u on CTA u % GRID).  Units below U_FULL are
@@ -216,6 +213,12 @@ struct GemmShape {
   static constexpr u32 UNITS = U_FULL + REM * TAIL;
 };
 static_assert(TCB_TAIL_SPLIT == 1 || TCB_SPLITK == 1, "tail split and split-K are exclusive");
+// The launch's control block at p[15]: the error word (16 bytes), then 4 arrival counters per split tile.
+__device__ __forceinline__ u32* tail_counters(const Args& a) { return reinterpret_cast<u32*>(a.p[15]) + 4; }
+__device__ __forceinline__ void clear_ctrl(const Args& a) {
+  u32* w = reinterpret_cast<u32*>(a.p[15]);
+  for (u32 i = threadIdx.x; i < 4 + 4 * GemmShape::REM; i += blockDim.x) w[i] = 0u;
+}
 static_assert(TCB_TAIL_SPLIT <= GemmShape::KB_ALL, "every tail unit has at least one k-block");
 
 // Row-major src [batch, R, C] -> hi, lo [batch, R, Kp] with Kp >= C (zero beyond C), 4 elements per step.
@@ -269,12 +272,7 @@ __device__ __forceinline__ void split_cols(const float* __restrict__ src, float*
 // A -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.  It runs first in every tensor-core
 // launch, so it also clears that launch's error word (p[15]) in the reused scratch.
 extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a) {
-  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
-    if (threadIdx.x == 0 && a.p[15]) *reinterpret_cast<u32*>(a.p[15]) = 0u;
-    // the tail units' arrival counters (one per tail tile and TMEM lane quarter)
-    u32* cnt = reinterpret_cast<u32*>(reinterpret_cast<unsigned char*>(a.scratch) + TCB_TAIL_CNT_OFFSET);
-    for (u32 i = threadIdx.x; i < 4 * tcb::GemmShape::REM; i += blockDim.x) cnt[i] = 0u;
-  }
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && a.p[15]) tcb::clear_ctrl(a);
   float* hi = reinterpret_cast<float*>(a.scratch);
   float* lo = hi + (u64)TCB_BATCH * TCB_M * TCB_KP;
   const float* src = reinterpret_cast<const float*>(a.in[TCB_IA]);
@@ -300,9 +298,7 @@ extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a)
 // With A split in the kernel there is no tcb_split_a: this one-block launch, first in the tensor-core
 // launch, clears its error word (p[15]) and the tail units' arrival counters instead.
 extern "C" __global__ void __launch_bounds__(128) tcb_gemm_prep(const tcb::Args a) {
-  if (threadIdx.x == 0 && a.p[15]) *reinterpret_cast<u32*>(a.p[15]) = 0u;
-  u32* cnt = reinterpret_cast<u32*>(reinterpret_cast<unsigned char*>(a.scratch) + TCB_TAIL_CNT_OFFSET);
-  for (u32 i = threadIdx.x; i < 4 * tcb::GemmShape::REM; i += blockDim.x) cnt[i] = 0u;
+  if (a.p[15]) tcb::clear_ctrl(a);
 }
 
 // Persistent: TCB_GRID CTAs (one per SM) walk the work units (grouped raster for L2 reuse); TMEM holds
@@ -544,7 +540,7 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
         __syncwarp();
         u32 old = 0;
         if (lane == 0)
-          old = atomicAdd(reinterpret_cast<u32*>(scr + TCB_TAIL_CNT_OFFSET) + 4 * (u32)T.tail + (u32)q, 1u);
+          old = atomicAdd(tail_counters(P.a) + 4 * (u32)T.tail + (u32)q, 1u);
         old = __shfl_sync(0xffffffffu, old, 0);
         if (old == S::TAIL - 1) {
           __threadfence();
@@ -571,7 +567,7 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
             finish16(T, row, c0, v);
           }
           // every piece has arrived: leave the counter at zero for the next launch
-          if (lane == 0) reinterpret_cast<u32*>(scr + TCB_TAIL_CNT_OFFSET)[4 * (u32)T.tail + (u32)q] = 0u;
+          if (lane == 0) tail_counters(P.a)[4 * (u32)T.tail + (u32)q] = 0u;
         }
         continue;
       }

@@ -56,13 +56,36 @@ extern "C" __global__ void __launch_bounds__(256) tcb_reduce_cols(const tcb::Arg
   }
 }
 
+// Combines the partials: a block takes 32 consecutive outputs (one per lane, so every load is a
+// coalesced 128-byte row); its 8 warps take the chunks s = w, w + 8, ... in order, and the 8 warp
+// results are combined in warp order -- a fixed order for every output, whatever the launch.
 extern "C" __global__ void __launch_bounds__(256) tcb_reduce_finish(const tcb::Args a) {
   const float* __restrict__ part = reinterpret_cast<const float*>(a.scratch);
   float* __restrict__ out = reinterpret_cast<float*>(a.out);
   constexpr u64 outs = (u64)TCB_OUTER * (u64)TCB_INNER;
-  for (u64 i = (u64)blockIdx.x * blockDim.x + threadIdx.x; i < outs; i += (u64)gridDim.x * blockDim.x) {
-    float acc = part[i];
-    for (int s = 1; s < TCB_SPLIT; ++s) acc = tcb::red_comb(acc, part[(u64)s * outs + i]);
-    out[i] = acc;
+  __shared__ float acc_w[8][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (u64 base = (u64)blockIdx.x * 32; base < outs; base += (u64)gridDim.x * 32) {
+    const u64 i = base + lane;
+    float acc = tcb::red_init();
+    if (i < outs) {
+      int s = w;
+      for (; s + 24 < TCB_SPLIT; s += 32) {  // four independent loads in flight
+        const float v0 = part[(u64)s * outs + i], v1 = part[(u64)(s + 8) * outs + i];
+        const float v2 = part[(u64)(s + 16) * outs + i], v3 = part[(u64)(s + 24) * outs + i];
+        acc = tcb::red_comb(acc, v0); acc = tcb::red_comb(acc, v1);
+        acc = tcb::red_comb(acc, v2); acc = tcb::red_comb(acc, v3);
+      }
+      for (; s < TCB_SPLIT; s += 8) acc = tcb::red_comb(acc, part[(u64)s * outs + i]);
+    }
+    acc_w[w][lane] = acc;
+    __syncthreads();
+    if (w == 0 && i < outs) {
+      float r = acc_w[0][lane];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) r = tcb::red_comb(r, acc_w[k][lane]);
+      out[i] = r;
+    }
+    __syncthreads();
   }
 }

@@ -64,7 +64,7 @@ class DPTrainer:
     """The transformer training step, data parallel.  `batch_local` sequences per rank."""
 
     def __init__(self, runner, V, batch_local, cfg, params, state=None, comm=None, opt=_steps.ADAM_3B,
-                 matmul="tiled", capture=True):
+                 matmul="tiled", capture=True, batch=True):
         self.runner, self.comm = runner, comm
         gs = _steps.build_grad3b(V, batch_local, cfg)
         ad = _steps.build_adam_graph(V, cfg, opt)
@@ -91,7 +91,7 @@ class DPTrainer:
         for gid, off in zip(grad_ids, offs):
             place_g[gid] = self.flat.ptr + off
         lowered_g = lower_fused(fg.graph, matmul=matmul, fold=True, keep=[self.loss_id, *grad_ids])
-        self.grad_prog = rt.Program(runner, fg.graph, lowered_g, keep=[self.loss_id], place=place_g)
+        self.grad_prog = rt.Program(runner, fg.graph, lowered_g, keep=[self.loss_id], place=place_g, batch=batch)
         fa = fuse(ad["graph"], keep=list(ad["outputs"].values()))
         place_a = {}
         for n, off in zip(names, offs):
@@ -101,7 +101,7 @@ class DPTrainer:
         feedback = [(fa.index[ad["outputs"][n]], fa.index[ad["inputs"][n]]) for n in names + state_names]
         self.adam_prog = rt.Program(runner, fa.graph, lower_fused(fa.graph, matmul=matmul),
                                     keep=[fa.index[ad["outputs"][k]] for k in names + state_names],
-                                    feedback=feedback, place=place_a)
+                                    feedback=feedback, place=place_a, batch=batch)
         self.fa, self.ad, self.fg, self.gs = fa, ad, fg, gs
         self.state_names = state_names
         for n in names:

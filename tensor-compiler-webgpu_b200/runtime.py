@@ -26,7 +26,7 @@ import numpy as np
 
 from . import build as _build
 from .ir import size
-from .codegen import lower, lower_fused, WG
+from .codegen import lower, lower_fused, WG, KernelCall
 
 TC_OK = 0
 STATUS = {0: "OK", 1: "INVALID", 2: "CUDA", 3: "COMPILE", 4: "OOM", 5: "TIMEOUT", 6: "NCCL", 7: "UNAVAILABLE"}
@@ -466,6 +466,81 @@ def plan_memory(sizes, first, last):
     return [off[i] for i in range(n)], total.value
 
 
+BATCH_MAX_ELEMS = 1 << 20   # elementwise launches up to this many elements may be batched
+
+
+class MultiLaunch:
+    """Same-source elementwise launches over different buffers issued as one `tcb_elementwise_multi`
+    launch (instance = blockIdx.y, argument blocks in a device table).  Stands at its last member's
+    position in a program's launch order."""
+
+    def __init__(self, members):
+        self.members = members
+        m0 = members[0]
+        self.code = m0.code
+        self.kind = "multi " + (m0.pattern or m0.kind)
+        self.pattern = m0.pattern
+        self.node = members[-1].node
+        self.nodes = [m.node for m in members]
+        self.inputs = [i for m in members for i in m.inputs]
+        self.scratch_bytes = 0
+        self.bytes = sum(m.bytes for m in members)
+        self.info = {"members": len(members)}
+        c = m0.calls[0]
+        gx = max(m.calls[0].grid[0] for m in members)   # the grid-stride loop covers every member's count
+        self.calls = [KernelCall("tcb_elementwise_multi", (gx, len(members), 1), c.block, c.smem, c.params)]
+
+
+def batch_small_launches(launches, root, max_elems=BATCH_MAX_ELEMS):
+    """Hoist small elementwise launches and batch the independent ones of one source.
+
+    Every small launch (a single tcb_elementwise call, no scratch, at most `max_elems` elements) moves
+    up to just after the launch that produces its last input: its slot is (anchor, depth), the anchor
+    being the last large producer among its inputs' producers and the depth one more than the deepest
+    small producer on that anchor.  Other launches keep their place, and moving a producer earlier
+    never puts it after a reader, so the order stays a valid one.  Small launches of one source that
+    land on the same slot cannot read one another (a reader is always deeper than what it reads) and
+    run as one MultiLaunch there.  Only small values live longer, so the arena grows little."""
+    def eligible(lau):
+        return (len(lau.calls) == 1 and lau.calls[0].name == "tcb_elementwise" and not lau.scratch_bytes
+                and lau.calls[0].err_offset is None and lau.calls[0].params and lau.calls[0].params[0] <= max_elems)
+    producer = {}
+    slot = []
+    for k, lau in enumerate(launches):
+        if eligible(lau):
+            best = (-1, 0)
+            for i in lau.inputs:
+                p = producer.get(root(i))
+                if p is not None:
+                    cand = (slot[p][0], slot[p][1] + 1) if slot[p][1] > 0 else (p, 1)
+                    best = max(best, cand)
+            if best[1] == 0:
+                best = (-1, 1)
+            slot.append(best)
+        else:
+            slot.append((k, 0))
+        producer[lau.node] = k
+    groups = {}
+    for k, lau in enumerate(launches):
+        if slot[k][1] > 0:
+            groups.setdefault((slot[k], lau.code), []).append(k)
+    rep = {}
+    for members in groups.values():
+        if len(members) > 1:
+            rep[members[0]] = MultiLaunch([launches[k] for k in members])
+            for k in members[1:]:
+                rep[k] = None
+    order = sorted(range(len(launches)), key=lambda k: (slot[k], k))
+    out = []
+    for k in order:
+        if k in rep:
+            if rep[k] is not None:
+                out.append(rep[k])
+        else:
+            out.append(launches[k])
+    return out
+
+
 class Program:
     """A lowered graph made resident on the device, replayed by a native plan.
 
@@ -477,11 +552,14 @@ class Program:
     feedback, src/gpu/trainer.js:64).
     """
 
-    def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False, place=None, alias=True):
+    def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False, place=None, alias=True,
+                 batch=False):
         """`place` maps node ids to device addresses owned by the caller (e.g. slices of one flat buffer).
 
         `alias`: a plain reshape launch is dropped and its value shares its source's memory (a row-major
         reshape moves no bytes); lifetimes are merged along alias chains.
+        `batch`: small independent launches of one elementwise source run as one launch
+        (`batch_small_launches`); values are unchanged, the number of launches drops.
         """
         self.runner = runner
         self.graph = graph
@@ -499,15 +577,18 @@ class Program:
                 self.alias[lau.node] = lau.inputs[0]
                 continue
             launches.append(lau)
-        self.launches = launches
 
         def root(i):
             while i in self.alias:
                 i = self.alias[i]
             return i
+        if batch:
+            launches = batch_small_launches(launches, root)
+        self.launches = launches
         first, last = {}, {}
         for k, lau in enumerate(self.launches):
-            first[lau.node] = k
+            for nid in getattr(lau, "nodes", [lau.node]):
+                first[nid] = k
             for i in lau.inputs:
                 r = root(i)
                 last[r] = max(last.get(r, -1), k)
@@ -544,29 +625,74 @@ class Program:
         self.scratch = DeviceBuffer(runner, scratch_bytes) if scratch_bytes else None
         if self.scratch:
             check(lib().tc_memset32(runner.ctx, self.scratch.ptr, 0, scratch_bytes // 4))
-        # one error word per launch that has one (launches share scratch, so not there)
+        # a private control block (error word + split-tile arrival counters) per launch that has one:
+        # launches share scratch, so not there.  The blocks start zeroed and stay so -- a bounded wait
+        # writes the error word only when it runs out (check_errors zeroes them again), the counters
+        # return to zero as each split tile completes -- so the one-block clearing launch
+        # (tcb_gemm_prep) that a one-off run needs is left out of the plan.
         self.err_slot = {}
+        off = 0
         for k, lau in enumerate(self.launches):
             if any(c.err_offset is not None for c in lau.calls):
-                self.err_slot[k] = len(self.err_slot)
-        self.errs = DeviceBuffer(runner, 4 * max(1, len(self.err_slot)))
-        check(lib().tc_memset32(runner.ctx, self.errs.ptr, 0, max(1, len(self.err_slot))))
+                self.err_slot[k] = off
+                off += (lau.info or {}).get("ctrl_bytes", 64)
+        self.errs_bytes = max(64, off)
+        self.errs = DeviceBuffer(runner, self.errs_bytes)
+        check(lib().tc_memset32(runner.ctx, self.errs.ptr, 0, self.errs_bytes // 4))
         h = ctypes.c_void_p()
         check(lib().tc_plan_create(runner.ctx, ctypes.byref(h)))
         self.plan = h
         self.kernel_launches = 0
+        self.tables = []
         for k, lau in enumerate(self.launches):
-            mod = runner.pipeline(lau.code)
-            ins = [self.ptrs[i] for i in lau.inputs]
-            for call in lau.calls:
-                issue(call, mod, ins, self.ptrs[lau.node], self.scratch.ptr if self.scratch else 0, plan=h,
-                      err_ptr=self.err_ptr(k))
+            for call in program_calls(lau):
+                self.issue_call(k, lau, call, h)
                 self.kernel_launches += 1
-        for src, dst in feedback:
-            check(lib().tc_plan_add_copy(h, self.ptrs[dst], self.ptrs[src], max(1, size(nodes[dst].shape)) * 4))
+        if batch and feedback:
+            self.kernel_launches += self._issue_copies(feedback, h)
+        else:
+            for src, dst in feedback:
+                check(lib().tc_plan_add_copy(h, self.ptrs[dst], self.ptrs[src], max(1, size(nodes[dst].shape)) * 4))
         self.captured = False
         if capture:
             self.capture()
+
+    def _issue_copies(self, feedback, plan):
+        """The feedback copies as one multi-instance copy launch per vector width; returns the launches."""
+        from .codegen import copy_source, grid1d
+        by_w = {}
+        for src, dst in feedback:
+            n = max(1, size(self.graph.nodes[dst].shape))
+            w = 4 if self.ptrs[src] % 16 == 0 and self.ptrs[dst] % 16 == 0 else 1
+            by_w.setdefault(w, []).append((self.ptrs[src], self.ptrs[dst], n))
+        for w, items in by_w.items():
+            mod = self.runner.pipeline(copy_source(w))
+            table = (Args * len(items))()
+            for j, (a, b, n) in enumerate(items):
+                table[j] = make_args([a], b, 0, [n])
+            buf = DeviceBuffer(self.runner, ctypes.sizeof(table))
+            check(lib().tc_upload(buf.handle, ctypes.addressof(table), ctypes.sizeof(table), 0))
+            self.tables.append(buf)
+            gx = max(grid1d(n, per_thread=w)[0] for _, _, n in items)
+            issue(KernelCall("tcb_elementwise_multi", (gx, len(items), 1), (WG, 1, 1), 0, [0]), mod, [], 0, buf.ptr,
+                  plan=plan)
+        return len(by_w)
+
+    def issue_call(self, k, lau, call, plan):
+        """Append one kernel call of launch `k` to a native plan (a MultiLaunch gets its argument table)."""
+        mod = self.runner.pipeline(lau.code)
+        scratch = self.scratch.ptr if self.scratch else 0
+        if isinstance(lau, MultiLaunch):
+            table = (Args * len(lau.members))()
+            for j, m in enumerate(lau.members):
+                table[j] = make_args([self.ptrs[i] for i in m.inputs], self.ptrs[m.node], 0, m.calls[0].params)
+            buf = DeviceBuffer(self.runner, ctypes.sizeof(table))
+            check(lib().tc_upload(buf.handle, ctypes.addressof(table), ctypes.sizeof(table), 0))
+            self.tables.append(buf)
+            issue(call, mod, [], 0, buf.ptr, plan=plan)
+            return
+        issue(call, mod, [self.ptrs[i] for i in lau.inputs], self.ptrs[lau.node], scratch, plan=plan,
+              err_ptr=self.err_ptr(k))
 
     def capture(self):
         check(lib().tc_plan_capture(self.plan))
@@ -599,19 +725,19 @@ class Program:
         check(lib().tc_plan_run(self.plan))
 
     def err_ptr(self, k):
-        return self.errs.ptr + 4 * self.err_slot[k] if k in self.err_slot else None
+        return self.errs.ptr + self.err_slot[k] if k in self.err_slot else None
 
     def check_errors(self):
         """Raise if any tensor-core launch's bounded wait ran out (its own error word, read after a sync)."""
         if not self.err_slot:
             return
         self.runner.sync()
-        w = self.errs.download(len(self.err_slot), np.uint32)
-        bad = [k for k, slot in self.err_slot.items() if w[slot]]
+        w = self.errs.download(self.errs_bytes // 4, np.uint32)
+        bad = [k for k, off in self.err_slot.items() if w[off // 4]]
         if bad:
-            check(lib().tc_memset32(self.runner.ctx, self.errs.ptr, 0, len(self.err_slot)))
+            check(lib().tc_memset32(self.runner.ctx, self.errs.ptr, 0, self.errs_bytes // 4))
             raise TcError(5, f"launch {bad[0]} ({self.launches[bad[0]].kind}): a bounded wait ran out "
-                             f"(code {int(w[self.err_slot[bad[0]]])})")
+                             f"(code {int(w[self.err_slot[bad[0]] // 4])})")
 
     def free(self):
         if self.plan:
@@ -626,6 +752,9 @@ class Program:
         if self.scratch:
             self.scratch.free()
             self.scratch = None
+        for b in getattr(self, "tables", []):
+            b.free()
+        self.tables = []
         if getattr(self, "errs", None):
             self.errs.free()
             self.errs = None
@@ -668,7 +797,7 @@ class GpuTrainer:
         names = list(params) + list(state)
         feedback = [(step["outputs"][n], step["inputs"][n]) for n in names]
         keep = {step["loss"], *[step["outputs"][n] for n in names]}
-        self.prog = Program(runner, graph, lowered, keep=keep, feedback=feedback)
+        self.prog = Program(runner, graph, lowered, keep=keep, feedback=feedback, batch=True)
         cot = graph.input_id(step["cotangent"])
         if cot is not None:
             self.prog.write(cot, [1.0])
@@ -699,25 +828,28 @@ class FusedTrainer(GpuTrainer):
         super().__init__(runner, step, params, state, capture=capture, lowered=step["lowered"])
 
 
+def program_calls(lau):
+    """The calls of a launch that a resident program issues: all but the control-block clearing."""
+    return [c for c in lau.calls if c.name != "tcb_gemm_prep"]
+
+
 class Segments:
     """Native plans over consecutive kernel-call ranges of a Program, so events can sit between them.
 
-    `cuts` are indices into the flat list of kernel calls (every call of every launch, in order).
+    `cuts` are indices into the flat list of kernel calls (every call of every launch, in order, as the
+    program issues them: `program_calls`).
     """
 
     def __init__(self, prog, cuts):
         self.prog = prog
         self.plans = []
-        flat = [(k, lau, call) for k, lau in enumerate(prog.launches) for call in lau.calls]
+        flat = [(k, lau, call) for k, lau in enumerate(prog.launches) for call in program_calls(lau)]
         bounds = [0, *cuts, len(flat)]
-        scratch = prog.scratch.ptr if prog.scratch else 0
         for a, b in zip(bounds[:-1], bounds[1:]):
             h = ctypes.c_void_p()
             check(lib().tc_plan_create(prog.runner.ctx, ctypes.byref(h)))
             for k, lau, call in flat[a:b]:
-                mod = prog.runner.pipeline(lau.code)
-                issue(call, mod, [prog.ptrs[i] for i in lau.inputs], prog.ptrs[lau.node], scratch, plan=h,
-                      err_ptr=prog.err_ptr(k))
+                prog.issue_call(k, lau, call, h)
             self.plans.append(h)
 
     def run(self, k):

@@ -106,7 +106,8 @@ def test_transpose_folding_picks_only_gemm_operand_transposes(pkg, cg):
 
 @pytest.mark.parametrize("shape", [(1, 4096, 4096, 4096), (1, 16384, 1024, 4096), (198, 128, 256, 128),
                                    (1, 5120, 256, 1024), (1, 2432, 128, 2048), (2048, 256, 64, 256),
-                                   (1, 256, 131072, 768), (3, 300, 96, 500)])
+                                   (1, 256, 131072, 768), (3, 300, 96, 500), (1, 16384, 256, 256),
+                                   (1, 2560, 1024, 512), (1, 256, 16384, 1024)])
 def test_gemm_last_wave_plan(cg, shape):
     """The persistent GEMM's unit schedule: every (tile, k-block) is covered exactly once, the last wave
     is split only when it would leave at least half the CTAs idle, and no CTA gets more than one
@@ -115,9 +116,13 @@ def test_gemm_last_wave_plan(cg, shape):
     bn = cg.gemm_bn(N)
     bk = cg.gemm_bk(bn)
     splitk, _ = cg.splitk_plan(batch, M, K, N, bn)
-    grid, tail, cnt_off, tail_off, end = cg.tail_plan(batch, M, K, N, bn, bk, splitk)
+    grid, tail, rem_plan, tail_off, end = cg.tail_plan(batch, M, K, N, bn, bk, splitk)
     tiles = batch * -(-M // cg.GEMM_BM) * -(-N // bn) * splitk
-    assert grid == min(cg.SM_COUNT, tiles)
+    if tiles < cg.SM_COUNT and splitk == 1:
+        assert grid == tiles * tail                  # every tile split, one K range per CTA
+    else:
+        assert grid == min(cg.SM_COUNT, tiles)
+    assert splitk == 1 or tiles // splitk <= cg.SM_COUNT // 9
     kb_all = cg._kpad(K) // bk
     rem = tiles % grid if tail > 1 else 0
     u_full = tiles - rem
@@ -140,4 +145,35 @@ def test_gemm_last_wave_plan(cg, shape):
     assert max(per_cta) - min(per_cta) <= 1
     if tail > 1:
         assert splitk == 1 and 2 * rem <= grid and kb_all // tail >= 4
-        assert tail_off >= cnt_off + 16 * rem and end == tail_off + rem * tail * cg.GEMM_BM * bn * 4
+        assert rem_plan == rem and tail_off >= cg.ctrl_bytes(rem)
+        assert end == tail_off + rem * tail * cg.GEMM_BM * bn * 4
+
+
+def test_batch_small_launches_keeps_dependencies():
+    """Small launches are hoisted to just after their last producer and same-source ones that land on
+    one slot are batched; every value is still produced before it is read, and large launches keep their
+    relative order."""
+    import importlib
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    cgm = importlib.import_module("tensor-compiler-webgpu_b200.codegen")
+
+    class L:
+        def __init__(self, node, inputs, code, n=1000):
+            self.node, self.inputs, self.code = node, inputs, code
+            self.calls = [cgm.KernelCall("tcb_elementwise", (4, 1, 1), (256, 1, 1), 0, [n])]
+            self.scratch_bytes, self.pattern, self.kind, self.bytes, self.info = 0, None, "e", 0, {}
+
+    # an Adam-like interleaving: per parameter j, m_j = M(g_j), v_j = V(g_j), p_j = P(m_j, v_j); then a
+    # large launch X reading p_0 and a small Q reading X
+    seq = []
+    for j in range(3):
+        seq += [L(100 + j, [j], "M"), L(200 + j, [j], "V"), L(300 + j, [100 + j, 200 + j], "P")]
+    seq += [L(400, [300], "X", n=1 << 22), L(401, [400], "M"), L(402, [5], "M")]
+    out = rt.batch_small_launches(seq, lambda i: i)
+    got = [sorted(getattr(x, "nodes", [x.node])) for x in out]
+    assert got == [[100, 101, 102, 402], [200, 201, 202], [300, 301, 302], [400], [401]]
+    pos = {n: k for k, x in enumerate(out) for n in getattr(x, "nodes", [x.node])}
+    for x in out:
+        for i in x.inputs:
+            if i in pos:
+                assert pos[i] < pos[x.node], (i, x.node)
