@@ -646,10 +646,10 @@ def gemm_smem(bn, bk=32):
     return gemm_stages(bn, bk) * gemm_stage_bytes(bn, bk) + 1024 + GEMM_STAGING + 1024
 
 
-def tma_store_ok(N, splitk):
-    """The epilogue writes through TMA stores when the output's row stride is a multiple of 16 bytes
-    (split-K launches write partial sums instead)."""
-    return N % 4 == 0 and splitk == 1
+def tma_store_ok(N, splitk=1):
+    """The epilogue writes through TMA stores (to the output, or with split-K to the partial sums) when a
+    row of N floats is a multiple of 16 bytes."""
+    return N % 4 == 0
 
 
 def gemm_bk(bn=128):
@@ -748,7 +748,7 @@ def fused_split_plan(batch, M, K, N, bn, a_t=False, b_t=False):
 
 
 def gemm_bn(N):
-    """Accumulator width: 256 TMEM columns when N fills them, else 128."""
+    """Accumulator width: 256 TMEM columns when N fills them, else 128 (TCB_GEMM_BN overrides)."""
     import os
     forced = os.environ.get("TCB_GEMM_BN")
     if forced:
@@ -794,7 +794,8 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
         maps += [("scratch", b_off, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn),
                  ("scratch", b_off + b_bytes, Kp, N, batch, Kp * 4, N * Kp * 4, bk, bn)]
     if tma_store_ok(N, splitk):
-        maps.append(("out", 0, N, M, batch, N * 4, M * N * 4, 32, 32))
+        maps.append(("out", 0, N, M, batch, N * 4, M * N * 4, 32, 32) if splitk == 1 else
+                    ("scratch", part_off, N, M, splitk * batch, N * 4, M * N * 4, 32, 32))
     gemm.tma = maps
     if fs[0]:
         first = KernelCall("tcb_gemm_prep", (1, 1, 1), (128, 1, 1))
@@ -812,8 +813,14 @@ def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabota
     lau = Launch(node_id, op, kind, pattern, inputs, code, calls, scratch_bytes=scratch,
                  info={"mnk": (batch, M, K, N), "bn": bn, "bk": bk, "stages": gemm_stages(bn, bk), "splitk": splitk,
                        "tail_split": tail, "ctrl_bytes": ctrl_bytes(rem), "fused_split": fs,
-                       "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t})
+                       "path": "tcgen05-3xtf32", "a_t": a_t, "b_t": b_t, "ia": ia, "ib": ib, "kp": Kp})
     return lau
+
+
+def split_multi_source():
+    """The module of tcb_split_multi (the operand splits of many GEMMs in one launch)."""
+    return '#include "tcb/common.cuh"\n#include "tcb/split.cuh"\n'
+
 
 
 # ------------------------------------------------------------------ plain reduce

@@ -571,11 +571,14 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
         }
         continue;
       }
-      if (TCB_TMA_STORE && TCB_SPLITK == 1) {
-        // 32 columns at a time: the fused body on this row's 32 values, written into a 128-byte-swizzled
-        // 32 x 32 staging block (conflict-free: 16-byte chunk c of row r at r * 128 + (c ^ (r & 7)) * 16),
-        // then one TMA store of the block; two blocks per warp alternate.
+      if (TCB_TMA_STORE) {
+        // 32 columns at a time: the fused body on this row's 32 values (split-K: the raw partial sums),
+        // written into a 128-byte-swizzled 32 x 32 staging block (conflict-free: 16-byte chunk c of row
+        // r at r * 128 + (c ^ (r & 7)) * 16), then one TMA store of the block -- to the output, or with
+        // split-K to this split's slice of the partial sums [SPLITK * batch, M, N]; two blocks per warp
+        // alternate.
         const int r = 32 * q + lane;
+        const int zc = TCB_SPLITK > 1 ? (int)(((t / S::TILES_PER) % TCB_SPLITK) * TCB_BATCH) + T.bz : T.bz;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32, ++nstore) {
           float v[32];
@@ -586,9 +589,13 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
           for (int jj = 0; jj < 32; ++jj) {
             const u64 col = (u64)(T.n0 + c0 + jj);
             const float acc = T.kb == 0 ? 0.0f : v[jj];
-            v[jj] = (grow < (u64)TCB_M && col < (u64)TCB_N)
-                        ? Epi::apply(P.a, acc, (u64)T.bz * TCB_M * TCB_N + grow * TCB_N + col, grow, col, (u64)T.bz)
-                        : 0.0f;
+            if (TCB_SPLITK > 1) {
+              v[jj] = acc;
+            } else {
+              v[jj] = (grow < (u64)TCB_M && col < (u64)TCB_N)
+                          ? Epi::apply(P.a, acc, (u64)T.bz * TCB_M * TCB_N + grow * TCB_N + col, grow, col, (u64)T.bz)
+                          : 0.0f;
+            }
           }
           const u32 blk = staging + (u32)((q * 2 + (nstore & 1)) * 4096);
           if (lane == 0 && nstore >= 2) bulk_wait_read1();
@@ -600,7 +607,7 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&P.maps[4], blk, T.n0 + c0, T.m0 + 32 * q, T.bz);
+            tma_store_3d(&P.maps[4], blk, T.n0 + c0, T.m0 + 32 * q, zc);
             bulk_commit();
           }
         }

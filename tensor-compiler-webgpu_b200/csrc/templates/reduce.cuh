@@ -26,7 +26,17 @@ extern "C" __global__ void __launch_bounds__(256) tcb_reduce_rows(const tcb::Arg
   for (u64 o = warp; o < (u64)TCB_OUTER; o += warps) {
     const float* row = x + o * (u64)TCB_N;
     float acc = tcb::red_init();
-    for (u64 k = lane; k < (u64)TCB_N; k += 32) acc = tcb::red_comb(acc, __ldg(row + k));
+    if constexpr (TCB_N % 4 == 0) {
+      // rows of a multiple of 4 floats start 16-byte aligned: 128-bit loads, 4 consecutive values per lane
+      const float4* r4 = reinterpret_cast<const float4*>(row);
+      for (u64 k = lane; k < (u64)TCB_N / 4; k += 32) {
+        const float4 v = __ldg(r4 + k);
+        acc = tcb::red_comb(acc, v.x); acc = tcb::red_comb(acc, v.y);
+        acc = tcb::red_comb(acc, v.z); acc = tcb::red_comb(acc, v.w);
+      }
+    } else {
+      for (u64 k = lane; k < (u64)TCB_N; k += 32) acc = tcb::red_comb(acc, __ldg(row + k));
+    }
     acc = TCB_IS_MAX ? tcb::warp_max(acc) : tcb::warp_sum(acc);
     if (lane == 0) out[o] = acc;
   }

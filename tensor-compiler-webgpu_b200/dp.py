@@ -48,8 +48,11 @@ class Comm:
         self.runner = runner
         self.rank, self.world = rank, world
 
-    def allreduce_mean(self, ptr, count):
-        rt.check(rt.lib().tc_allreduce_f32(self.handle, ptr, count, ctypes.c_float(1.0 / self.world)))
+    def allreduce_mean(self, ptr, count, prescaled=False):
+        """Sum-allreduce, scaled by 1/W inside the collective (NCCL PreMulSum) unless the values were
+        scaled already (`prescaled`: then a plain sum, which NCCL can also run as an NVLS reduction)."""
+        scale = 1.0 if prescaled else 1.0 / self.world
+        rt.check(rt.lib().tc_allreduce_f32(self.handle, ptr, count, ctypes.c_float(scale)))
 
     def wait(self, timeout_ms=COMM_TIMEOUT_MS):
         rt.check(rt.lib().tc_comm_wait(self.handle, timeout_ms))
@@ -110,8 +113,13 @@ class DPTrainer:
             state = _steps.adam_initial_state(names, shapes)
         for k in state_names:
             self.adam_prog.write(fa.index[ad["inputs"][k]], state[k])
+        # With a power-of-two world the 1/W of the mean goes into the cotangent seed: backpropagation is
+        # linear in it and a power-of-two scale is exact in every operation, so each rank's gradients
+        # come out as exactly 1/W times its own, and the allreduce is a plain sum.
         cot = fg.graph.input_id(gs["cotangent"])
-        self.grad_prog.write(cot, [1.0])
+        w = comm.world if comm is not None else 1
+        self.prescaled = w > 1 and (w & (w - 1)) == 0
+        self.grad_prog.write(cot, [1.0 / w if self.prescaled else 1.0])
         self.x_id = fg.index[gs["inputs"]["x"]]
         self.y_id = fg.index[gs["inputs"]["y"]]
         self.kernel_launches = self.grad_prog.kernel_launches + self.adam_prog.kernel_launches
@@ -123,7 +131,7 @@ class DPTrainer:
         """One step with x, y already on the device: gradients, allreduce, Adam (asynchronous)."""
         self.grad_prog.run()
         if self.comm is not None and self.comm.world > 1:
-            self.comm.allreduce_mean(self.flat.ptr, self.flat_floats)
+            self.comm.allreduce_mean(self.flat.ptr, self.flat_floats, prescaled=self.prescaled)
         self.adam_prog.run()
 
     def train(self, x, y):

@@ -223,6 +223,8 @@ def _map_desc(call, scratch, ins=(), out=0):
             addr = ins[off]
         elif region == "out":
             addr = out + off
+        elif region == "abs":
+            addr = off
         else:
             raise ValueError(f"tensor map over '{region}'")
         if addr % 16:
@@ -644,8 +646,15 @@ class Program:
         self.plan = h
         self.kernel_launches = 0
         self.tables = []
+        self.split_bufs = []
+        self.hoisted = {}
+        self._hoist = None
+        if batch:
+            self.kernel_launches += self._hoist_input_splits(h)
         for k, lau in enumerate(self.launches):
             for call in program_calls(lau):
+                if k in self.hoisted and call.name == "tcb_split_b":
+                    continue
                 self.issue_call(k, lau, call, h)
                 self.kernel_launches += 1
         if batch and feedback:
@@ -656,6 +665,47 @@ class Program:
         self.captured = False
         if capture:
             self.capture()
+
+    def _hoist_input_splits(self, plan):
+        """Split every tensor-core launch's B operand that no launch of this program produces (a
+        program input: the weights of a training step) in one tcb_split_multi launch at the start of
+        the plan, into buffers of their own; those launches skip their split_b pass and their GEMM
+        reads B_hi / B_lo there.  Returns the launches added (0 or 1)."""
+        from .codegen import split_multi_source, grid1d
+        produced = set()
+        for lau in self.launches:
+            produced.update(getattr(lau, "nodes", [lau.node]))
+        jobs = []
+        for k, lau in enumerate(self.launches):
+            info = lau.info or {}
+            if info.get("path") != "tcgen05-3xtf32" or not any(c.name == "tcb_split_b" for c in lau.calls):
+                continue
+            b_node = lau.inputs[info["ib"]]
+            r = b_node
+            while r in self.alias:
+                r = self.alias[r]
+            if r in produced:
+                continue
+            batch, M, K, N = info["mnk"]
+            kp = info["kp"]
+            nbytes = batch * N * kp * 4
+            buf = DeviceBuffer(self.runner, 2 * nbytes)
+            self.split_bufs.append(buf)
+            self.hoisted[k] = (buf.ptr, buf.ptr + nbytes)
+            jobs.append((self.ptrs[b_node], buf.ptr, buf.ptr + nbytes, batch, N, K, kp, 0 if info["b_t"] else 1))
+        if not jobs:
+            return 0
+        table = (ctypes.c_uint64 * (8 * len(jobs)))(*[v for j in jobs for v in j])
+        tbuf = DeviceBuffer(self.runner, ctypes.sizeof(table))
+        check(lib().tc_upload(tbuf.handle, ctypes.addressof(table), ctypes.sizeof(table), 0))
+        self.tables.append(tbuf)
+        gx = 1
+        for src, hi, lo, b, R, C, kp, cols in jobs:
+            gx = max(gx, grid1d(b * R * kp, per_thread=1)[0] if not cols else min(b * (kp // 32) * -(-R // 32), 148 * 8))
+        mod = self.runner.pipeline(split_multi_source())
+        self._hoist = (KernelCall("tcb_split_multi", (gx, len(jobs), 1), (256, 1, 1), 0, []), mod, tbuf.ptr)
+        issue(self._hoist[0], mod, [], 0, tbuf.ptr, plan=plan)
+        return 1
 
     def _issue_copies(self, feedback, plan):
         """The feedback copies as one multi-instance copy launch per vector width; returns the launches."""
@@ -691,6 +741,15 @@ class Program:
             self.tables.append(buf)
             issue(call, mod, [], 0, buf.ptr, plan=plan)
             return
+        if k in self.hoisted and call.tma:
+            # this GEMM's B_hi / B_lo were split at the start of the plan into buffers of their own
+            hi, lo = self.hoisted[k]
+            tma = list(call.tma)
+            tma[2] = ("abs", hi) + tuple(tma[2][2:])
+            tma[3] = ("abs", lo) + tuple(tma[3][2:])
+            orig = call
+            call = KernelCall(orig.name, orig.grid, orig.block, orig.smem, orig.params)
+            call.tma, call.err_offset = tma, orig.err_offset
         issue(call, mod, [self.ptrs[i] for i in lau.inputs], self.ptrs[lau.node], scratch, plan=plan,
               err_ptr=self.err_ptr(k))
 
@@ -752,9 +811,10 @@ class Program:
         if self.scratch:
             self.scratch.free()
             self.scratch = None
-        for b in getattr(self, "tables", []):
+        for b in getattr(self, "tables", []) + getattr(self, "split_bufs", []):
             b.free()
         self.tables = []
+        self.split_bufs = []
         if getattr(self, "errs", None):
             self.errs.free()
             self.errs = None
@@ -843,11 +903,14 @@ class Segments:
     def __init__(self, prog, cuts):
         self.prog = prog
         self.plans = []
-        flat = [(k, lau, call) for k, lau in enumerate(prog.launches) for call in program_calls(lau)]
+        flat = [(k, lau, call) for k, lau in enumerate(prog.launches) for call in program_calls(lau)
+                if not (k in prog.hoisted and call.name == "tcb_split_b")]
         bounds = [0, *cuts, len(flat)]
         for a, b in zip(bounds[:-1], bounds[1:]):
             h = ctypes.c_void_p()
             check(lib().tc_plan_create(prog.runner.ctx, ctypes.byref(h)))
+            if a == 0 and prog._hoist is not None:  # the program's up-front operand splits
+                issue(prog._hoist[0], prog._hoist[1], [], 0, prog._hoist[2], plan=h)
             for k, lau, call in flat[a:b]:
                 prog.issue_call(k, lau, call, h)
             self.plans.append(h)

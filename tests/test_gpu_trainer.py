@@ -149,3 +149,34 @@ def test_streamed_program_matches_step_by_step(pkg, runner):
         for hin, hout in hosts:
             for h in list(hin.values()) + list(hout.values()):
                 h.free()
+
+
+def test_batched_program_changes_no_bit(pkg, runner):
+    """The data-parallel trainer with its resident programs batched (small same-source launches as one
+    multi-instance launch, the weight operand splits hoisted into one launch, the feedback copies as
+    one launch) against the same trainer unbatched: bit for bit, and with fewer launches."""
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    dp = importlib.import_module("tensor-compiler-webgpu_b200.dp")
+    s = pkg.steps
+    cfg, c = wl.c5_cfg(d=64, L=2, H=4, ff=128, T=32, batch=4)
+    V, B = c["V"], c["batch"]
+    params = s.init_params_normal(V, 0, 0.02, cfg)
+    x, y = wl.one_hot_batch(wl.c5_tokens(B, cfg["T"], V), V)
+    a = dp.DPTrainer(runner, V, B, cfg, params, batch=False)
+    b = dp.DPTrainer(runner, V, B, cfg, params, batch=True)
+    try:
+        assert b.kernel_launches < a.kernel_launches
+        assert b.grad_prog.hoisted and any(isinstance(l, pkg_runtime().MultiLaunch) for l in b.adam_prog.launches)
+        for _ in range(2):
+            la, lb = a.train(x, y), b.train(x, y)
+            assert np.float32(la).view(np.uint32) == np.float32(lb).view(np.uint32)
+        pa, pb = a.read(a.names), b.read(b.names)
+        for k in a.names:
+            assert np.array_equal(pa[k].view(np.uint32), pb[k].view(np.uint32)), k
+    finally:
+        a.destroy()
+        b.destroy()
+
+
+def pkg_runtime():
+    return importlib.import_module("tensor-compiler-webgpu_b200.runtime")
