@@ -365,6 +365,37 @@ def _tf32x3_peak():
         return round(1590.0 / 2 / 3, 1), "fallback bf16 1.59 PF / 2 / 3"
 
 
+def step_roofline(launches, hbm_gbs, tensor_tflops):
+    """The ideal time of a whole step: every launch at its own roofline -- a GEMM at the slower of its
+    useful flops / the tensor ceiling and its algorithmic bytes / HBM, every other launch at its
+    algorithmic bytes / HBM -- summed in milliseconds, with the split into the two kinds."""
+    t_tensor = t_hbm = 0.0
+    flops = nbytes = 0
+    for lau in launches:
+        info = getattr(lau, "info", None) or {}
+        if "mnk" in info:
+            b, M, K, N = info["mnk"]
+            f = 2 * b * M * N * K
+            flops += f
+            t_tensor += max(f / (tensor_tflops * 1e12), lau.bytes / (hbm_gbs * 1e9))
+        else:
+            t_hbm += lau.bytes / (hbm_gbs * 1e9)
+        nbytes += lau.bytes
+    return {"ideal_ms": round((t_tensor + t_hbm) * 1e3, 3), "gemm_ms": round(t_tensor * 1e3, 3),
+            "hbm_ms": round(t_hbm * 1e3, 3), "matmul_tflop": round(flops / 1e12, 3), "algorithmic_gb": round(nbytes / 1e9, 2)}
+
+
+def _sustained_peaks():
+    """(HBM GB/s, 3xTF32 TFLOP/s) for a kernel timed inside a long step: the measured copy rate and the
+    measured sustained bf16 dense rate / 2 / 3."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])) / 6, "measured"
+    except Exception:
+        return 6650.0, 1400.0 / 6, "fallback"
+
+
 def _code_hash(code):
     """Hash of a launch's source plus the text of every library template it includes, so a
     recorded traffic figure is used only for the exact kernel it was captured on."""
@@ -552,6 +583,8 @@ def run_c5(args):
     tokens = B * T
     value = tokens / (ms / 1e3)
     flops = _matmul_flops(pkg, tr.fg.graph) * world
+    hbm, tfl, peak_kind = _sustained_peaks()
+    sr = step_roofline(list(tr.grad_prog.launches) + list(tr.adam_prog.launches), hbm, tfl)
     # end to end: this rank's x, y from pinned host memory, the step, the loss back to the host
     hx, hy = rt.PinnedHost(x.nbytes), rt.PinnedHost(y.nbytes)
     hx.array(x.size)[:] = x
@@ -588,6 +621,9 @@ def run_c5(args):
         "roofline": {"bound": "tensor", "achieved": round(flops / (ms / 1e3) / 1e12, 2), "peak": None,
                      "unit": "TFLOP/s", "frac": None, "traffic": None,
                      "kernel": "whole step: matmul FLOPs / step time (3xTF32 tcgen05 contractions)"},
+        "step_roofline": dict(sr, frac=round(sr["ideal_ms"] / ms, 4), peaks=f"{peak_kind}: HBM {hbm:.1f} GB/s, "
+                              f"3xTF32 {tfl:.1f} TFLOP/s (sustained bf16 / 2 / 3)",
+                              how="per rank: each launch of the gradient and Adam programs at its own roofline, summed"),
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * x.nbytes,
                 "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 3)},
         "gpu_launches": K * tr.kernel_launches,

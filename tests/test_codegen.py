@@ -177,3 +177,27 @@ def test_batch_small_launches_keeps_dependencies():
         for i in x.inputs:
             if i in pos:
                 assert pos[i] < pos[x.node], (i, x.node)
+
+
+def test_c5_step_roofline(pkg, cg):
+    """bench.step_roofline on the C5 programs: the GEMMs' useful flops are the model's (about 2.9
+    TFLOP per 131,072-token step) and the ideal step lies between the pure-HBM and pure-tensor bounds."""
+    import importlib
+    import sys
+    import os
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    bench = importlib.import_module("bench")
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    cfg, c = wl.c5_cfg(batch=512)
+    V = c["V"]
+    gs = pkg.steps.build_grad3b(V, 512, cfg)
+    names = gs["names"]
+    keep = [gs["loss"], *[gs["grads"][n] for n in names]]
+    fg = pkg.fuse.fuse(gs["graph"], keep=keep)
+    grad_ids = [fg.index[gs["grads"][n]] for n in names]
+    low = cg.lower_fused(fg.graph, matmul="tiled", fold=True, keep=[fg.index[gs["loss"]], *grad_ids])
+    sr = bench.step_roofline(low["launches"], 6558.1, 1396.5 / 6)
+    assert 2.8 < sr["matmul_tflop"] < 3.0
+    assert sr["hbm_ms"] > 0 and sr["gemm_ms"] >= sr["matmul_tflop"] / (1396.5 / 6) * 1e3 - 1e-6
+    assert abs(sr["ideal_ms"] - sr["gemm_ms"] - sr["hbm_ms"]) < 1e-2
+    assert 30 < sr["ideal_ms"] < 50
