@@ -1,0 +1,241 @@
+"""Resident programs built on the CPU against a recording stand-in of the device library.
+
+`Program` turns a lowered graph into a native plan: arena offsets from value lifetimes, reshapes
+aliased, small same-source launches hoisted and batched (`batch=True`), the weights' operand splits
+hoisted into one launch, per-launch control blocks.  These tests build the trainers' real programs
+with `lib()` replaced by a recorder (device addresses from a bump allocator; the arena planner is
+the library's own `tc_plan_memory`, which needs no device) and then replay the recorded order on
+the host, tracking which value each byte of device memory holds:
+
+* every launch reads only values that are still in place (no arena reuse clobbers a live value, in
+  the reordered, batched plan as in the plain one);
+* the launches batched together neither read nor overlap one another's outputs;
+* the argument tables uploaded for batched launches and hoisted splits carry the right addresses.
+"""
+import ctypes
+import importlib
+
+import numpy as np
+import pytest
+
+
+class Recorder:
+    """The subset of the C ABI a Program uses, recorded instead of executed."""
+
+    def __init__(self, real):
+        self.real = real
+        self.next_addr = 1 << 40
+        self.buffers = {}          # handle -> (address, bytes)
+        self.uploads = {}          # address -> bytes uploaded
+        self.plans = {}            # plan handle -> entries
+        self._h = 100
+
+    def _handle(self):
+        self._h += 1
+        return self._h
+
+    def tc_last_error(self):
+        return b"recorder"
+
+    def tc_alloc(self, ctx, nbytes, canary, out):
+        h = self._handle()
+        addr = self.next_addr
+        self.next_addr += (int(nbytes) + 255) // 256 * 256 + 256
+        self.buffers[h] = (addr, int(nbytes))
+        out._obj.value = h
+        return 0
+
+    def tc_buf_ptr(self, h, out):
+        out._obj.value = self.buffers[h if isinstance(h, int) else h.value][0]
+        return 0
+
+    def tc_free(self, h):
+        return 0
+
+    def tc_memset32(self, ctx, ptr, value, count):
+        return 0
+
+    def tc_upload(self, h, host, nbytes, offset):
+        addr = self.buffers[h if isinstance(h, int) else h.value][0]
+        self.uploads[addr + int(offset)] = ctypes.string_at(host, int(nbytes))
+        return 0
+
+    def tc_memcpy_htod(self, ctx, dst, host, nbytes):
+        return 0
+
+    def tc_sync(self, ctx, timeout):
+        return 0
+
+    def tc_plan_create(self, ctx, out):
+        h = self._handle()
+        self.plans[h] = []
+        out._obj.value = h
+        return 0
+
+    def _args(self, a):
+        a = a._obj
+        return {"in": list(a.in_), "out": a.out, "scratch": a.scratch, "p": list(a.p)}
+
+    def tc_plan_add_launch(self, plan, mod, name, grid, block, smem, args):
+        self.plans[plan.value].append(("launch", name.decode(), tuple(grid), self._args(args), None))
+        return 0
+
+    def tc_plan_add_launch_tma(self, plan, mod, name, grid, block, smem, n, desc, args):
+        maps = [tuple(desc[8 * m + j] for j in range(8)) for m in range(n)]
+        self.plans[plan.value].append(("launch", name.decode(), tuple(grid), self._args(args), maps))
+        return 0
+
+    def tc_plan_add_copy(self, plan, dst, src, nbytes):
+        self.plans[plan.value].append(("copy", int(dst), int(src), int(nbytes)))
+        return 0
+
+    def tc_plan_capture(self, plan):
+        return 0
+
+    def tc_plan_free(self, plan):
+        return 0
+
+    def tc_plan_memory(self, *a):
+        return self.real.tc_plan_memory(*a)
+
+
+@pytest.fixture()
+def recorded(pkg, monkeypatch):
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    rec = Recorder(rt.lib())
+    monkeypatch.setattr(rt, "lib", lambda: rec)
+    monkeypatch.setattr(rt.GpuRunner, "pipeline", lambda self, code: rt.Module(hash(code) & 0xFFFF, self))
+    return rt, rec, rt.GpuRunner(1, 0)
+
+
+def _replay(prog, graph):
+    """Walk the program's launches in plan order, tracking which value each byte range holds."""
+    nodes = graph.nodes
+
+    def root(i):
+        while i in prog.alias:
+            i = prog.alias[i]
+        return i
+
+    def rng(i):
+        r = root(i)
+        return prog.ptrs[r], prog.ptrs[r] + max(1, int(np.prod(nodes[r].shape, dtype=np.int64))) * 4
+
+    holder = []        # (lo, hi, node) of values in memory
+    valid = set()
+    for n in nodes:
+        if n.op in ("input", "const") and n.id in prog.ptrs:
+            holder.append((*rng(n.id), root(n.id)))
+            valid.add(root(n.id))
+
+    def write(i):
+        lo, hi = rng(i)
+        for (a, b, v) in list(holder):
+            if a < hi and lo < b and v != root(i):
+                valid.discard(v)
+        holder.append((lo, hi, root(i)))
+        valid.add(root(i))
+
+    for lau in prog.launches:
+        members = getattr(lau, "members", [lau])
+        outs = [m.node for m in members]
+        for m in members:
+            for i in m.inputs:
+                if nodes[root(i)].op in ("input", "const"):
+                    continue
+                assert root(i) in valid, f"launch of node {m.node} reads node {i} after its memory was reused"
+        if len(members) > 1:
+            spans = [rng(o) for o in outs]
+            reads = [rng(i) for m in members for i in m.inputs]
+            for k, (a, b) in enumerate(spans):
+                for j, (c, d) in enumerate(spans):
+                    assert j == k or b <= c or d <= a, "batched outputs overlap"
+                for (c, d) in reads:
+                    if c < b and a < d:
+                        assert (c, d) == (a, b), "a batched launch writes what another member reads"
+        for o in outs:
+            write(o)
+
+
+def _dp_trainer(pkg, runner, batch):
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    dp = importlib.import_module("tensor-compiler-webgpu_b200.dp")
+    cfg, c = wl.c5_cfg(d=64, L=2, H=4, ff=128, T=32, batch=4)
+    V, B = c["V"], c["batch"]
+    params = pkg.steps.init_params_normal(V, 0, 0.02, cfg)
+    return dp.DPTrainer(runner, V, B, cfg, params, batch=batch, capture=False)
+
+
+@pytest.mark.parametrize("batch", [False, True])
+def test_plans_never_read_a_reused_value(pkg, recorded, batch):
+    rt, rec, runner = recorded
+    tr = _dp_trainer(pkg, runner, batch)
+    _replay(tr.grad_prog, tr.fg.graph)
+    _replay(tr.adam_prog, tr.fa.graph)
+
+
+def test_batched_plan_tables_and_hoisted_splits(pkg, recorded):
+    rt, rec, runner = recorded
+    tr = _dp_trainer(pkg, runner, True)
+    ap = tr.adam_prog
+    multis = [l for l in ap.launches if isinstance(l, rt.MultiLaunch)]
+    cg = importlib.import_module("tensor-compiler-webgpu_b200.codegen")
+    assert multis and 2 * len(ap.launches) < len(cg.lower_fused(tr.fa.graph, matmul="tiled")["launches"])
+    entries = rec.plans[ap.plan.value]
+    launches = [e for e in entries if e[0] == "launch"]
+    assert len(launches) == ap.kernel_launches
+    # each batched launch's table: one argument block per member, with that member's addresses
+    multi_calls = [e for e in launches if e[1] == "tcb_elementwise_multi"]
+    for lau in multis:
+        call = next(e for e in multi_calls if e[2][1] == len(lau.members)
+                    and rec.uploads.get(e[3]["scratch"]) is not None
+                    and rt.Args.from_buffer_copy(rec.uploads[e[3]["scratch"]][:ctypes.sizeof(rt.Args)]).out
+                    == ap.ptrs[lau.members[0].node])
+        raw = rec.uploads[call[3]["scratch"]]
+        table = (rt.Args * len(lau.members)).from_buffer_copy(raw)
+        for j, m in enumerate(lau.members):
+            assert table[j].out == ap.ptrs[m.node]
+            assert [table[j].in_[k] for k in range(len(m.inputs))] == [ap.ptrs[i] for i in m.inputs]
+            assert table[j].p[0] == m.calls[0].params[0]
+    # the gradient program: one up-front split launch whose jobs read the weights and fill the
+    # buffers the hoisted GEMMs' B maps point at; those GEMMs issue no split_b of their own
+    gp = tr.grad_prog
+    assert gp.hoisted
+    g_entries = [e for e in rec.plans[gp.plan.value] if e[0] == "launch"]
+    assert g_entries[0][1] == "tcb_split_multi"
+    jobs = np.frombuffer(rec.uploads[g_entries[0][3]["scratch"]], dtype=np.uint64).reshape(-1, 8)
+    assert len(jobs) == len(gp.hoisted)
+    split_targets = {(int(j[1]), int(j[2])) for j in jobs}
+    assert split_targets == set(gp.hoisted.values())
+    for k, (hi, lo) in gp.hoisted.items():
+        lau = gp.launches[k]
+        b = lau.inputs[lau.info["ib"]]
+        assert any(int(j[0]) == gp.ptrs[b] and (int(j[1]), int(j[2])) == (hi, lo) for j in jobs)
+    gemms = [e for e in g_entries if e[1] == "tcb_gemm_tc"]
+    hoisted_maps = [e[4] for e in gemms if (e[4][2][0], e[4][3][0]) in split_targets]
+    assert len(hoisted_maps) == len(gp.hoisted)
+    n_split_b = sum(1 for e in g_entries if e[1] == "tcb_split_b")
+    n_split_b_lowered = sum(1 for lau in gp.launches for c in lau.calls if c.name == "tcb_split_b")
+    assert n_split_b == n_split_b_lowered - len(gp.hoisted)
+    # no one-block clearing launches in a resident plan; every GEMM has its own control block
+    assert all(e[1] != "tcb_gemm_prep" for e in g_entries)
+    ctrl = [e[3]["p"][15] for e in gemms]
+    assert len(set(ctrl)) == len(ctrl) and all(c for c in ctrl)
+
+
+def test_replay_catches_a_clobbered_value(pkg, recorded, monkeypatch):
+    """The replay is not vacuous: with an arena planner that puts every value at offset 0 it finds a
+    hazard (batched outputs on top of one another, or a launch reading a value whose memory was
+    reused)."""
+    rt, rec, runner = recorded
+
+    def all_at_zero(n, nbytes, first, last, offsets, total):
+        for k in range(n):
+            offsets[k] = 0
+        total._obj.value = max(int(nbytes[k]) for k in range(n)) if n else 0
+        return 0
+
+    monkeypatch.setattr(rec, "tc_plan_memory", all_at_zero)
+    tr = _dp_trainer(pkg, runner, True)
+    with pytest.raises(AssertionError, match="memory was reused|overlap"):
+        _replay(tr.grad_prog, tr.fg.graph)
