@@ -157,19 +157,20 @@ def _replay(prog, graph):
             write(o)
 
 
-def _dp_trainer(pkg, runner, batch):
+def _dp_trainer(pkg, runner, batch, full=False):
     wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
     dp = importlib.import_module("tensor-compiler-webgpu_b200.dp")
-    cfg, c = wl.c5_cfg(d=64, L=2, H=4, ff=128, T=32, batch=4)
+    cfg, c = wl.c5_cfg(batch=512) if full else wl.c5_cfg(d=64, L=2, H=4, ff=128, T=32, batch=4)
     V, B = c["V"], c["batch"]
     params = pkg.steps.init_params_normal(V, 0, 0.02, cfg)
     return dp.DPTrainer(runner, V, B, cfg, params, batch=batch, capture=False)
 
 
-@pytest.mark.parametrize("batch", [False, True])
-def test_plans_never_read_a_reused_value(pkg, recorded, batch):
+@pytest.mark.parametrize("batch,full", [(False, False), (True, False), (True, True)])
+def test_plans_never_read_a_reused_value(pkg, recorded, batch, full):
+    """Small model plain and batched, and the C5 benchmark's own programs (global batch 512)."""
     rt, rec, runner = recorded
-    tr = _dp_trainer(pkg, runner, batch)
+    tr = _dp_trainer(pkg, runner, batch, full)
     _replay(tr.grad_prog, tr.fg.graph)
     _replay(tr.adam_prog, tr.fa.graph)
 
