@@ -154,5 +154,42 @@ def test_gemm_operand_layouts(pkg, oracle, runner, wl, cg, monkeypatch, a_t, b_t
     assert j["pass"], j
 
 
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (True, True)])
+def test_gemm_last_wave_split_with_in_kernel_operand_split(pkg, oracle, runner, cg, a_t, b_t):
+    """150 batched 128 x 256 x 64 products: 150 tiles on 148 CTAs, so the last two tiles are cut into K
+    ranges, while both operands are split inside the GEMM (each is loaded by one tile): judged against
+    the oracle."""
+    from importlib import import_module
+    ir = import_module("tensor-compiler-webgpu_b200.ir")
+    Bt, M, K, N = 150, 128, 256, 64
+    g = ir.Graph()
+    x = g.input("x", [Bt, K, M] if a_t else [Bt, M, K])
+    y = g.input("y", [Bt, N, K] if b_t else [Bt, K, N])
+    a = g.transpose(x, [0, 2, 1]) if a_t else x
+    b = g.transpose(y, [0, 2, 1]) if b_t else y
+    out = g.relu(g.matmul(a, b))
+    rng = pkg.rng.Rng(11)
+    inputs = {"x": rng.normal_array(Bt * M * K, 0, K ** -0.5).astype(np.float32),
+              "y": rng.normal_array(Bt * K * N, 0, K ** -0.5).astype(np.float32)}
+    values, bounds, rounded = oracle.reference_with_bounds(g, inputs)
+    fused = pkg.fuse.fuse(g, keep=[out])
+    o = fused.index[out]
+    lowered = cg.lower_fused(fused.graph, matmul="tiled", fold=True, keep=[o])
+    tc = [l for l in lowered["launches"] if l.info and l.info.get("path") == "tcgen05-3xtf32"]
+    assert [(l.info["tail_split"] > 1, l.info["fused_split"]) for l in tc] == [(True, (True, True))]
+    prog = pkg_runtime().Program(runner, fused.graph, lowered, keep=[o])
+    try:
+        for n in fused.graph.inputs():
+            prog.write(n.id, rounded[n.attrs["name"]].astype(np.float32))
+        prog.run()
+        runner.sync()
+        prog.check_errors()
+        got = prog.read(o)
+    finally:
+        prog.free()
+    j = oracle.judge_outputs([values[out]], [bounds[out]], [got])
+    assert j["pass"], j
+
+
 def pkg_runtime():
     return importlib.import_module("tensor-compiler-webgpu_b200.runtime")
