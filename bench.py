@@ -397,15 +397,18 @@ def _sustained_peaks():
 
 
 def _code_hash(code):
-    """Hash of a launch's source plus the text of every library template it includes, so a
-    recorded traffic figure is used only for the exact kernel it was captured on."""
+    """Hash of a launch's source plus the code of every library template it includes (their `//`
+    comments and blank lines left out), so a recorded traffic figure is used only for the exact
+    kernel it was captured on, and a comment edit does not orphan it."""
     import hashlib
     import re
     h = hashlib.sha256(code.encode())
     tdir = os.path.join(ROOT, "tensor-compiler-webgpu_b200", "csrc", "templates")
     for name in sorted(set(re.findall(r'#include "tcb/([a-z_]+\.cuh)"', code))):
-        with open(os.path.join(tdir, name), "rb") as f:
-            h.update(f.read())
+        with open(os.path.join(tdir, name)) as f:
+            text = f.read()
+        lines = (ln.rstrip() for ln in re.sub(r"//[^\n]*", "", text).splitlines())
+        h.update("\n".join(ln for ln in lines if ln).encode())
     return h.hexdigest()[:16]
 
 

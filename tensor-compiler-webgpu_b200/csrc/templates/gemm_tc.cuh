@@ -2,27 +2,38 @@
 // (class 2 of the fusion pass on its tensor-core path; the reference's WGSL
 // forms are src/gpu/codegen.js:152-193 and src/fusion/codegen-fused.js:176-265).
 //
-// float32 accuracy from TF32 units by the 3xTF32 split: every operand value x
-// is written as hi = rna_tf32(x) and lo = rna_tf32(x - hi), and
-//   A.B ~= A_lo.B_hi + A_hi.B_lo + A_hi.B_hi     (A_lo.B_lo, ~2^-24 |ab|, dropped)
-// accumulated in float32 in tensor memory.  The split is two small kernels
-// (tcb_split_a: A -> A_hi, A_lo; tcb_split_b: B -> B_hi^T, B_lo^T, transposed
-// so both operands are K-major) writing into scratch, zero padded to Kp, a
-// multiple of 32.  The GEMM kernel then:
-//   warp 0   TMA producer: 128-byte-swizzled [rows x 32] fp32 tiles of the four
-//            split operands into a STAGES-deep shared-memory ring (mbarriers);
-//   warp 1   allocates BN TMEM columns, and one lane issues
-//            tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=BN, K=8), 12 per
-//            32-wide k-block, committing each stage back to the producer;
-//   warps 2-5 epilogue: tcgen05.ld of the accumulator rows (warp w reads TMEM
-//            lanes 32*(w%4)..), the fused body (bias, activation, residual ...)
-//            on each value, float4 stores.
+// float32 accuracy from TF32 units by the 3xTF32 split of every operand value x
+// into hi and lo, accumulated in float32 in tensor memory:
+//   A.B ~= A_lo.B_hi + A_hi.B_lo + A_hi.B_hi     (A_lo.B_lo dropped)
+// An operand is split either by a pass into scratch (tcb_split_a / tcb_split_b:
+// hi = rna_tf32(x), lo = rna_tf32(x - hi), K-major, zero padded to Kp, a
+// multiple of 32) or, when few output tiles load it (TCB_FS_A / TCB_FS_B), in
+// the kernel: its raw tile arrives by TMA (K-major, or MN-major in the 128-byte
+// swizzle of 32-byte chunks) and serves as hi -- the tensor core reads an fp32
+// operand as tf32 by dropping 13 mantissa bits -- and lo = rna_tf32(x -
+// trunc(x)) is written beside it in shared memory.
+//
+// tcb_gemm_tc is persistent: TCB_GRID CTAs (one per SM) walk work units --
+// 128 x BN output tiles in grouped raster order, the last wave's tiles (or all
+// tiles, when fewer than the SMs) cut into K ranges whose partial tiles the
+// last-arriving warp sums in range order -- with warps specialised:
+//   warp 0     TMA producer: the stage's operand tiles into a STAGES-deep ring;
+//   warp 1     allocates 2 x BN TMEM columns (two accumulators) and one lane
+//              issues tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=BN, K=8),
+//              three per K step, committing each stage back to the producer;
+//   warps 2-5  epilogue: tcgen05.ld of one accumulator while the MMA warp fills
+//              the other, the fused body (bias, activation, residual ...) on
+//              each value, 32 x 32 blocks staged in swizzled shared memory and
+//              written by TMA stores (split-K: the partial sums);
+//   warps 6-9  (in-kernel split only) the lo tiles of each stage.
 // No TMA multicast.  Every wait is bounded by the global timer; a wait that
-// runs out sets the error word (scratch + err_offset) and the kernel unwinds,
+// runs out sets the launch's error word (p[15]) and the kernel unwinds,
 // freeing its TMEM.
 //
 // The generated part defines TCB_M, TCB_N, TCB_K, TCB_KP, TCB_BATCH, TCB_IA,
-// TCB_IB, TCB_BN, TCB_STAGES and struct Epi (as for tcb/matmul.cuh).
+// TCB_IB, TCB_BN, TCB_BK, TCB_STAGES, TCB_SPLITK, TCB_GRID, TCB_TAIL_SPLIT,
+// TCB_FS_A, TCB_FS_B, TCB_TMA_STORE, the scratch offsets and struct Epi (as for
+// tcb/matmul.cuh).
 #pragma once
 
 namespace tcb {
