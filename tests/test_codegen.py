@@ -201,3 +201,32 @@ def test_c5_step_roofline(pkg, cg):
     assert sr["hbm_ms"] > 0 and sr["gemm_ms"] >= sr["matmul_tflop"] / (1396.5 / 6) * 1e3 - 1e-6
     assert abs(sr["ideal_ms"] - sr["gemm_ms"] - sr["hbm_ms"]) < 1e-2
     assert 30 < sr["ideal_ms"] < 50
+
+
+@pytest.mark.parametrize("a_t,b_t,mode", [(False, False, "1"), (True, False, "1"), (False, True, "a"),
+                                          (True, True, "b"), (False, False, "0")])
+def test_gemm_variants_compile_for_sm100a(pkg, cg, monkeypatch, a_t, b_t, mode):
+    """Every tensor-core GEMM variant compiles with NVRTC for sm_100a (no device needed): operands
+    K-major or MN-major, split in the kernel or by a pass, with a last-wave split, with split-K, with
+    and without the TMA-store epilogue."""
+    import importlib
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    ir = importlib.import_module("tensor-compiler-webgpu_b200.ir")
+    monkeypatch.setenv("TCB_GEMM_FUSED", mode)
+    for Bt, M, K, N in ((150, 128, 256, 64), (1, 256, 4096, 128), (2, 300, 96, 130)):
+        g = ir.Graph()
+        x = g.input("x", [Bt, K, M] if a_t else [Bt, M, K])
+        y = g.input("y", [Bt, N, K] if b_t else [Bt, K, N])
+        a = g.transpose(x, [0, 2, 1]) if a_t else x
+        b = g.transpose(y, [0, 2, 1]) if b_t else y
+        out = g.tanh(g.matmul(a, b))
+        f = pkg.fuse.fuse(g, keep=[out])
+        for lau in cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=[f.index[out]])["launches"]:
+            assert rt.compile_check(lau.code) > 0
+
+
+def test_multi_instance_modules_compile(cg):
+    import importlib
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    for src in (cg.copy_source(4), cg.copy_source(1), cg.split_multi_source()):
+        assert rt.compile_check(src) > 0
