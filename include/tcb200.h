@@ -164,7 +164,10 @@ int tc_plan_memory(int n, const uint64_t* bytes, const int32_t* first_use, const
  *      all calls and needs no clearing (every partial is written before it is read);
  *      calls that overlap on the GPU race on it.  The first call on a device looks up
  *      the array's address with that device current: make it before any stream
- *      capture.  `stream` is a CUstream / cudaStream_t handle (0 = legacy default). ---- */
+ *      capture.  The current device must be the one `in` and `out` live on (else
+ *      TC_ERR_INVALID), and `stream` (a CUstream / cudaStream_t handle, 0 = legacy
+ *      default) must belong to it.  For cols > 1 the sums are bitwise those of the
+ *      regular `sum` over axis 0 launch of the same matrix. ---- */
 int tc_colsum_f32_static(uint64_t in, uint64_t out, uint64_t rows, uint64_t cols, uint64_t stream);
 
 /* ---- data-parallel collectives (NCCL, loaded at run time) ---- */

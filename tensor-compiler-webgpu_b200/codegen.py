@@ -834,7 +834,8 @@ def _reduce_source(op, in_shape, axis):
     outs = outer * inner
     split = 1
     if inner > 1 and outs < 2 * SM_COUNT * 256 and n >= 64:
-        split = max(1, min(math.ceil(n / 32), math.ceil(SM_COUNT * 2048 / max(1, outs))))
+        # at most 65535 chunks: the chunk index is the grid's y coordinate
+        split = max(1, min(math.ceil(n / 32), math.ceil(SM_COUNT * 2048 / max(1, outs)), 65535))
     src = f"""// {op} over axis {axis} of {list(in_shape)}: outer {outer}, n {n}, inner {inner}, split {split}
 #include "tcb/common.cuh"
 #define TCB_OUTER {outer}

@@ -84,13 +84,44 @@ def fuzz_sources(every=10):
     return codes
 
 
-def warm(full=True, prune=True):
-    """Compile the standard kernels into the cache; with `prune`, drop cached cubins of other sources
-    (old templates or codegen) so the cache that travels with the tree stays small."""
+def full_size_sources():
+    """Kernels of the BASELINE configs at full size (C2, C3 both shapes with relu and tanh, C4 softmax,
+    logSoftmax and row sum) and of the value sabotages over the direct cases."""
+    codes = set()
+    W = wl.c2_graph(8192, 8192)
+    codes |= _codes(W["graph"], W["keep"])
+    for M, K, N in wl.C3_SHAPES:
+        for act in ("relu", "tanh"):
+            W = wl.c3_graph(M, K, N, act)
+            codes |= _codes(W["graph"], W["keep"], "tiled")
+    for what in ("softmax", "logsoftmax", "rowsum"):
+        W = wl.c4_graph(65536, 4096, what)
+        codes |= _codes(W["graph"], W["keep"])
+    for c in fused_direct_cases():
+        f = fuse(c["graph"])
+        for s in ("epilogue-before-bias", "layernorm-tree-short", "softmax-no-max"):
+            codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul=c.get("matmul", "naive"),
+                                                         sabotage=s)["launches"]}
+    return codes
+
+
+def graph_sources(graphs):
+    """Kernels of (graph, keep) pairs on both matmul paths, fused and unfused."""
+    codes = set()
+    for g, keep in graphs:
+        for mm in ("naive", "tiled"):
+            codes |= _codes(g, keep, mm)
+    return codes
+
+
+def warm(full=True, prune=True, extra=()):
+    """Compile the standard kernels (and the sources in `extra`) into the cache; with `prune`, drop
+    cached cubins of other sources (old templates or codegen) so the cache that travels with the tree
+    stays small."""
     import os
-    codes = standard_sources(full)
+    codes = standard_sources(full) | set(extra)
     if full:
-        codes |= sweep_sources() | fuzz_sources(10)
+        codes |= sweep_sources() | fuzz_sources(10) | full_size_sources()
     n = rt.precompile(codes)
     if prune and full and os.path.isdir(rt.CACHE_DIR):
         keep = {os.path.basename(rt._cache_path(c)) for c in codes}

@@ -114,3 +114,52 @@ def test_a_rank_that_never_joins_fails_the_others_with_an_error():
     p.join(60)
     assert not p.is_alive()
     assert q.get(timeout=5) != "joined"
+
+
+def _prescaled_worker(rank, world, port, q):
+    """The product's algebra for a power-of-two world (dp.py): each rank seeds its loss cotangent with 1/W
+    instead of 1, and the allreduce is a plain sum with no division afterwards."""
+    _setup(rank, world, port)
+    import oracle
+    pkg = importlib.import_module("tensor-compiler-webgpu_b200")
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    s = pkg.steps
+    cfg, c = wl.c5_cfg(d=16, L=1, H=2, ff=32, T=8, batch=4)
+    V, B = c["V"], c["batch"]
+    bl = B // world
+    params = s.init_params_normal(V, 0, 0.02, cfg)
+    toks = wl.c5_tokens(B, cfg["T"], V)[rank * bl:(rank + 1) * bl]
+    x, y = wl.one_hot_batch(toks, V)
+    gs = s.build_grad3b(V, bl, cfg)
+    feed = {**params, "x": x, "y": y}
+    seeded = oracle.evaluate(gs["graph"], {**feed, gs["cotangent"]: [1.0 / world]})
+    plain = oracle.evaluate(gs["graph"], {**feed, gs["cotangent"]: [1.0]})
+    mine = np.concatenate([seeded[gs["grads"][n]] for n in gs["names"]])
+    unit = np.concatenate([plain[gs["grads"][n]] for n in gs["names"]])
+    t = torch.from_numpy(mine.copy())
+    dist.all_reduce(t)  # a plain sum: the 1/W is already inside every rank's gradients
+    if rank == 0:  # small messages only: the parent reads the queue after the ranks have exited
+        q.put((t.numpy(), bool(np.array_equal(mine, unit / world))))
+    dist.destroy_process_group()
+
+
+def test_prescaled_seed_plain_sum_gives_the_full_batch_gradient(oracle, pkg):
+    """Backpropagation is linear in the cotangent seed and a power-of-two scale is exact in every
+    floating-point operation (away from underflow), so seeding with 1/W gives exactly 1/W times the
+    unit-seed gradients, bit for bit; their plain sum over the ranks is the full-batch gradient."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    mp.start_processes(_prescaled_worker, args=(world, _port(), q), nprocs=world, start_method="spawn", join=True)
+    got, exact = q.get(timeout=10)
+    assert exact
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    s = pkg.steps
+    cfg, c = wl.c5_cfg(d=16, L=1, H=2, ff=32, T=8, batch=4)
+    V, B = c["V"], c["batch"]
+    params = s.init_params_normal(V, 0, 0.02, cfg)
+    x, y = wl.one_hot_batch(wl.c5_tokens(B, cfg["T"], V), V)
+    gs = s.build_grad3b(V, B, cfg)
+    vals = oracle.evaluate(gs["graph"], {**params, "x": x, "y": y, gs["cotangent"]: [1.0]})
+    want = np.concatenate([vals[gs["grads"][n]] for n in gs["names"]])
+    np.testing.assert_allclose(got, want, rtol=1e-9, atol=1e-14)
