@@ -263,6 +263,38 @@ class _EwLoads:
         return ref
 
 
+def _ew_body_struct(body, out_id, n):
+    """The `struct Body` of an elementwise body (load plan + straight-line compute), shared by the
+    elementwise and the elementwise + column-sum templates."""
+    T = idx_type(n)
+    loads = _EwLoads("W", T)
+    em = Emitter(body, loads.leaf)
+    base = Ctx("i")
+    out = em.value(out_id, base)
+    fields = "\n    ".join(loads.fields) or "float unused_;"
+    stmts = "\n    ".join(loads.stmts)
+    lanes = "\n      ".join(loads.per_lane)
+    per_lane = f"#pragma unroll\n    for (int l = 0; l < W; ++l) {{\n      {lanes}\n    }}" if loads.per_lane else ""
+    comp = "\n      ".join(em.lines)
+    return f"""struct Body {{
+  template <int W> struct Regs {{
+    {fields}
+  }};
+  template <int W> __device__ __forceinline__ static void load(const tcb::Args& a, u64 i0, Regs<W>& r) {{
+    {stmts}
+    {per_lane}
+  }}
+  template <int W> __device__ __forceinline__ static void compute(const Regs<W>& r, float (&o)[W]) {{
+#pragma unroll
+    for (int l = 0; l < W; ++l) {{
+      {comp}
+      o[l] = {out};
+    }}
+  }}
+}};
+"""
+
+
 def _elementwise_source(body, out_id, n, sabotage=None, tag="elementwise"):
     T = idx_type(n)
     loads = _EwLoads("W", T)
@@ -855,14 +887,17 @@ class KernelCall:
     ``tma``: tensor maps to build at launch, each (region, offset, cols, rows, batches, row_stride_bytes,
     batch_stride_bytes, box_cols, box_rows) with region 'scratch' (offset = bytes into scratch), 'in'
     (offset = the launch operand's index) or 'out'; ``err_offset``: where in scratch the
-    kernel's error word lives (its address goes in p[15]).
+    kernel's error word lives (its address goes in p[15]).  A launch with two outputs (an elementwise
+    value and its column sum) names the second through ``out_node`` / ``ptr_params``.
     """
-    __slots__ = ("name", "grid", "block", "smem", "params", "tma", "err_offset")
+    __slots__ = ("name", "grid", "block", "smem", "params", "tma", "err_offset", "out_node", "ptr_params")
 
     def __init__(self, name, grid, block, smem=0, params=()):
         self.name, self.grid, self.block, self.smem, self.params = name, tuple(grid), tuple(block), smem, list(params)
         self.tma = None
         self.err_offset = None
+        self.out_node = None     # a node whose buffer is this call's `out` instead of the launch's node
+        self.ptr_params = ()     # (k, node): p[k] gets that node's device address
 
     def __repr__(self):
         return f"KernelCall({self.name}, grid={self.grid}, block={self.block})"
@@ -871,7 +906,8 @@ class KernelCall:
 class Launch:
     """One node's work: the reference's launch record ``{node, op, kind, pattern, inputs, params, grid, code}``
     (src/gpu/lower.js:108-111, src/fusion/lower-fused.js:37-41) with CUDA source and kernel calls."""
-    __slots__ = ("node", "op", "kind", "pattern", "inputs", "code", "calls", "scratch_bytes", "bytes", "info")
+    __slots__ = ("node", "op", "kind", "pattern", "inputs", "code", "calls", "scratch_bytes", "bytes", "info",
+                 "nodes")   # `nodes`: every node a launch with two outputs produces (unset otherwise)
 
     def __init__(self, node, op, kind, pattern, inputs, code, calls, scratch_bytes=0, info=None):
         self.node, self.op, self.kind, self.pattern = node, op, kind, pattern
@@ -1096,6 +1132,83 @@ def lower(graph, matmul="naive", sabotage=None, fold=False, keep=()):
     return {"launches": launches, "folded": sorted(folds)}
 
 
+# ------------------------------------------------------------------ elementwise + column sum
+def _elementwise_producer(node):
+    if node.op == "fused":
+        return node.attrs["kind"] == "elementwise"
+    return node.op in _BIN or node.op in _UN
+
+
+def colsum_fusions(graph, keep=()):
+    """Column sums to fuse with their producer: {sum id: (producer id, write)}.
+
+    A `sum` over axis 0 of a value with more than one column whose producer is an elementwise launch (a
+    fused elementwise node or a plain elementwise op) is computed in the producer's pass over the
+    tensor (tcb/colsum.cuh).  `write`: the producer's value is kept or read by another node, so the
+    fused launch still stores it; otherwise it is never materialised.  The reference's pass leaves these
+    sums plain (src/fusion/fuse.js:43-45)."""
+    keep = set(keep)
+    consumers = {}
+    for n in graph.nodes:
+        for i in n.inputs:
+            consumers.setdefault(i, []).append(n.id)
+    out, taken = {}, set()
+    for S in graph.nodes:
+        if S.op != "sum" or S.attrs["axis"] != 0:
+            continue
+        P = graph.nodes[S.inputs[0]]
+        if P.id in taken or len(P.shape) < 2 or size(P.shape[1:]) <= 1 or not _elementwise_producer(P):
+            continue
+        out[S.id] = (P.id, P.id in keep or len(consumers[P.id]) > 1)
+        taken.add(P.id)
+    return out
+
+
+def _colsum_launch(graph, P, S, write):
+    """One launch computing elementwise node P over [R, C] and S = sum over axis 0 of it (tcb/colsum.cuh),
+    with the plain column sum's split, so the sum is bitwise the unfused pair's."""
+    from .fuse import body_of
+    if P.op == "fused":
+        body, out_id = body_of(P), P.attrs["output"]
+    else:
+        body, out_id = _one_op_body(P.op, [graph.nodes[i].shape for i in P.inputs], P.attrs)
+    R, C = P.shape[0], size(P.shape[1:])
+    _, (_, _, _, split) = _reduce_source("sum", list(P.shape), 0)
+    # 128-bit lanes only when the split already gives every SM a full complement of threads; the plain
+    # sum's split aims at one thread per column and chunk (148 x 2048), which single lanes keep
+    W = 4 if C % 4 == 0 and (C // 4) * split >= SM_COUNT * 1024 else 1
+    src = f"""// elementwise ({P.op}) + column sum over axis 0 of [{R}, {C}], split {split}, value {'stored' if write else 'not stored'}
+#include "tcb/common.cuh"
+#define TCB_OUTER 1
+#define TCB_N {R}
+#define TCB_INNER {C}
+#define TCB_SPLIT {split}
+#define TCB_IS_MAX 0
+#define TCB_W {W}
+#define TCB_WRITE {int(write)}
+{_ew_body_struct(body, out_id, R * C)}#include "tcb/colsum.cuh"
+"""
+    groups = C // W
+    block = min(256, max(32, -(-groups // 32) * 32))
+    main = KernelCall("tcb_ew_colsum", (max(1, min(math.ceil(groups / block), SM_COUNT * 8)), split, 1), (block, 1, 1))
+    calls = [main]
+    if write and split == 1:
+        main.ptr_params = ((14, S.id),)
+    if split > 1:
+        fin = KernelCall("tcb_reduce_finish", (max(1, min(math.ceil(C / 32), SM_COUNT * 8)), 1, 1), (256, 1, 1))
+        if write:
+            fin.out_node = S.id
+        calls.append(fin)
+    lau = Launch(P.id if write else S.id, "fused", "fused-colsum", "elementwise+colsum", list(P.inputs), src, calls,
+                 scratch_bytes=split * C * 4 if split > 1 else 0,
+                 info={"R": R, "C": C, "split": split, "write": write, "producer": P.id, "sum": S.id})
+    if write:
+        lau.nodes = [P.id, S.id]
+    nbytes = sum(size(graph.nodes[i].shape) * 4 for i in dict.fromkeys(P.inputs)) + C * 4
+    lau.bytes = nbytes + (R * C * 4 if write else 0)
+    return lau
+
+
 def fused_kernel(node, matmul="naive", sabotage=None):
     """The launch of a fused node (src/fusion/codegen-fused.js:357-362)."""
     from .fuse import body_of
@@ -1114,17 +1227,32 @@ def fused_kernel(node, matmul="naive", sabotage=None):
     raise ValueError(f"no fused kernel kind '{kind}'")
 
 
-def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=()):
+def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfuse=False):
     """A fused node to its kernel, every other node to its plain launch (src/fusion/lower-fused.js:32-45).
 
     `fold` (resident programs only): transposeLast2 nodes read only as tensor-core GEMM operands get no
     launch; the GEMM's operand split reads their source.  Their values then never exist on the device,
     so verification runs that read back every node lower without it.
+    `colfuse` (resident programs only): a sum over axis 0 runs in its elementwise producer's launch
+    (colsum_fusions); a producer read by nothing else is then never stored.  `keep` names the values
+    that must exist after the launches.
     """
     folds = foldable_transposes(graph, matmul, keep) if fold else set()
+    cols = colsum_fusions(graph, keep) if colfuse else {}
+    producer_of = {p: (sid, w) for sid, (p, w) in cols.items()}
     launches = []
     for node in graph.nodes:
         if node.op in ("input", "const") or node.id in folds:
+            continue
+        if node.id in producer_of:        # the producer of a fused column sum
+            sid, write = producer_of[node.id]
+            if write:
+                launches.append(_colsum_launch(graph, node, graph.nodes[sid], True))
+            continue
+        if node.id in cols:               # the column sum itself
+            pid, write = cols[node.id]
+            if not write:
+                launches.append(_colsum_launch(graph, graph.nodes[pid], node, False))
             continue
         ops = _matmul_operands(graph, node) if folds else None
         if ops and set(ops) & folds:

@@ -233,13 +233,20 @@ def _map_desc(call, scratch, ins=(), out=0):
     return (ctypes.c_uint64 * len(vals))(*vals)
 
 
-def issue(call, mod, ins, out, scratch, plan=None, err_ptr=None):
+def issue(call, mod, ins, out, scratch, plan=None, err_ptr=None, ptrs=None):
     """Launch one KernelCall now (plan None) or append it to a native plan.
 
     A call with an error word gets its address in p[15]: `err_ptr` when given (a resident program's own
-    word for that launch), else its slot in the scratch buffer.
+    word for that launch), else its slot in the scratch buffer.  `ptrs` (node id -> device address)
+    resolves a call's `out_node` and `ptr_params` (a launch with a second output).
     """
     params = list(call.params)
+    if call.out_node is not None:
+        out = ptrs[call.out_node]
+    for k, nid in call.ptr_params:
+        while len(params) <= k:
+            params.append(0)
+        params[k] = ptrs[nid]
     if call.err_offset is not None:
         while len(params) < 16:
             params.append(0)
@@ -369,12 +376,13 @@ class GpuRunner:
     def sync(self, timeout_ms=SYNC_TIMEOUT_MS):
         check(lib().tc_sync(self.ctx, int(timeout_ms)))
 
-    def launch(self, lau, in_ptrs, out_ptr):
-        """Issue every kernel call of one Launch (asynchronous)."""
+    def launch(self, lau, in_ptrs, out_ptr, ptrs=None):
+        """Issue every kernel call of one Launch (asynchronous); `ptrs` maps node ids to device addresses
+        for a launch with a second output."""
         mod = self.pipeline(lau.code)
         scratch = self.scratch(lau.scratch_bytes)
         for call in lau.calls:
-            issue(call, mod, in_ptrs, out_ptr, scratch)
+            issue(call, mod, in_ptrs, out_ptr, scratch, ptrs=ptrs)
         return scratch
 
     def run(self, graph, lowered, inputs, canary=False):
@@ -402,8 +410,9 @@ class GpuRunner:
                         else np.asarray(v, dtype=np.float32)
                     bufs[node.id].upload(arr)
             checks = []
+            ptrs = {node.id: bufs[node.id].ptr for node in graph.nodes}
             for lau in lowered["launches"]:
-                sc = self.launch(lau, [bufs[i].ptr for i in lau.inputs], bufs[lau.node].ptr)
+                sc = self.launch(lau, [bufs[i].ptr for i in lau.inputs], bufs[lau.node].ptr, ptrs)
                 if any(c.err_offset is not None for c in lau.calls):
                     self.sync()
                     self.check_errors(lau, sc)
@@ -521,7 +530,8 @@ def batch_small_launches(launches, root, max_elems=BATCH_MAX_ELEMS):
             slot.append(best)
         else:
             slot.append((k, 0))
-        producer[lau.node] = k
+        for nid in getattr(lau, "nodes", None) or [lau.node]:   # a two-output launch produces both
+            producer[nid] = k
     groups = {}
     for k, lau in enumerate(launches):
         if slot[k][1] > 0:
@@ -555,8 +565,12 @@ class Program:
     """
 
     def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False, place=None, alias=True,
-                 batch=False):
+                 batch=False, prune=True):
         """`place` maps node ids to device addresses owned by the caller (e.g. slices of one flat buffer).
+
+        `prune`: launches whose values nothing reads -- no kept, fed-back or caller-placed value depends
+        on them (autodiff's branches toward constants, say) -- are left out; every value the program
+        exposes is unchanged.
 
         `alias`: a plain reshape launch is dropped and its value shares its source's memory (a row-major
         reshape moves no bytes); lifetimes are merged along alias chains.
@@ -572,7 +586,17 @@ class Program:
         fb = {i for pair in feedback for i in pair}
         self.alias = {}
         launches = []
+        live = None
+        if prune:
+            live = set(keep) | {src for src, _ in feedback} | set(place)
+            for n in reversed(nodes):
+                if n.id in live:
+                    live.update(n.inputs)
+        self.pruned = 0
         for lau in lowered["launches"]:
+            if live is not None and not any(n in live for n in getattr(lau, "nodes", [lau.node])):
+                self.pruned += 1
+                continue
             n = nodes[lau.node]
             if (alias and n.op == "reshape" and lau.kind == "gather" and lau.node not in keep
                     and lau.node not in place and lau.node not in fb):
@@ -751,7 +775,7 @@ class Program:
             call = KernelCall(orig.name, orig.grid, orig.block, orig.smem, orig.params)
             call.tma, call.err_offset = tma, orig.err_offset
         issue(call, mod, [self.ptrs[i] for i in lau.inputs], self.ptrs[lau.node], scratch, plan=plan,
-              err_ptr=self.err_ptr(k))
+              err_ptr=self.err_ptr(k), ptrs=self.ptrs)
 
     def capture(self):
         check(lib().tc_plan_capture(self.plan))

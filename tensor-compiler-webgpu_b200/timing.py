@@ -16,6 +16,9 @@ src/fusion/workloads.js on the B200.
   and softmax rows, broadcast-recompute, lost reuse, the model's forward and step -- as unfused,
   fused, recompute and matmul-only variants.  The third-party hand-written kernels of the reference's
   sweep are not part of this backend.
+* ``gate`` (web/m4-bench.html:116-146): before a workload is timed, each variant runs once and its
+  outputs are judged against the float64 reference (a judge the caller supplies); a variant that fails
+  is not timed.
 * ``ceiling_programs`` (workloads.js:305-345): pure-read and copy kernels over 128 MiB, 32/64/128-bit
   elements, 256 / 1024 / 4096 CTAs of 256 threads, grid-strided: the measured HBM ceiling.
 """
@@ -212,7 +215,8 @@ def _graph_workload(wid, family, params, build, variants=("unfused", "fused"), m
         outs = build(g)
         outs = list(outs) if isinstance(outs, (list, tuple)) else [outs]
         return g, outs, _draw_inputs(g, seed, ranges)
-    return {"id": wid, "family": family, "params": params, "variants": list(variants), "matmul": matmul, "make": make}
+    return {"id": wid, "family": family, "params": params, "variants": list(variants), "matmul": matmul, "make": make,
+            "judge": "composed"}
 
 
 def _binary_chain(g, n, L):
@@ -292,7 +296,8 @@ def _model_workload(what, V, B):
                                                                     "y": onehot(targets), st["cotangent"]: [1.0]}
     variants = ("unfused", "fused", "matmul-only") if what == "step" else ("unfused", "fused")
     return {"id": f"{what}-V{V}-B{B}", "family": "training-step" if what == "step" else "forward",
-            "params": {"V": V, "B": B}, "variants": list(variants), "matmul": "naive", "make": make}
+            "params": {"V": V, "B": B}, "variants": list(variants), "matmul": "naive", "make": make,
+            "judge": "compare"}
 
 
 def build_variants(w):
@@ -365,8 +370,42 @@ def ceiling_programs():
     return out
 
 
-def run_sweep(bench, only=None, families=None, log=None):
-    """Time every workload's variants and the ceiling programs; returns a list of result records."""
+def compare_outputs(a, b):
+    """The model workloads' gate (workloads.js:370-374): the largest difference between two variants'
+    outputs, and whether all are finite."""
+    diffs = [float(np.max(np.abs(x.astype(np.float64) - y))) if x.size else 0.0 for x, y in zip(a, b)]
+    finite = all(np.isfinite(x).all() for x in a) and all(np.isfinite(x).all() for x in b)
+    return {"finite": bool(finite), "maxAbs": max(diffs) if diffs else 0.0, "lossDiff": diffs[0] if diffs else 0.0}
+
+
+def gate(bench, w, v, prepared, judge):
+    """Each variant once, its outputs judged before anything is timed (web/m4-bench.html:116-146).
+
+    `judge(graph, inputs, outputs, gpu_outputs) -> {"pass", ...}` judges one variant's outputs against
+    the float64 reference with amendment 8's composed bound (workloads.js:275-301 streamingReference,
+    :351-367 judgeOutputs); the caller supplies it (the checker is test infrastructure, not part of this
+    package).  The model workloads, whose composed bound is vacuous, compare fused with unfused instead."""
+    outs = {name: bench.outputs(p) for name, p in prepared.items() if name != "matmul-only"}
+    g = {}
+    if w.get("judge", "composed") == "composed":
+        for name, o in outs.items():
+            j = judge(v["graph"], v["inputs"], v["outputs"], o)
+            g[name] = {k: j.get(k) for k in ("pass", "unjudged", "worst", "unjudgeable", "elements", "first")}
+    else:
+        c = compare_outputs(outs["fused"], outs["unfused"])
+        g["fusedVsUnfused"] = c
+        g["fused"] = {"pass": c["finite"]}
+        g["unfused"] = {"pass": all(np.isfinite(x).all() for x in outs["unfused"])}
+    failed = [k for k, r in g.items() if r.get("pass") is False]
+    return {"pass": not failed, "failed": failed, "variants": g}
+
+
+def run_sweep(bench, only=None, families=None, log=None, judge=None):
+    """Time every workload's variants and the ceiling programs; returns a list of result records.
+
+    Every workload is gated first (`gate`): a variant whose outputs fail the judge is not timed."""
+    if judge is None:
+        raise ValueError("run_sweep needs a judge: every variant's outputs are checked before it is timed")
     results = []
     for c in ceiling_programs():
         if only and not any(s in c["id"] for s in only):
@@ -386,9 +425,20 @@ def run_sweep(bench, only=None, families=None, log=None):
             continue
         v = build_variants(w)
         prepared = {name: bench.prepare(p) for name, p in v["programs"].items()}
+        gt = gate(bench, w, v, prepared, judge)
+        if not gt["pass"]:
+            results.append({"id": w["id"], "family": w["family"], "params": w["params"], "gate": gt,
+                            "failedGate": gt["failed"], "created": {}, "variants": {}})
+            for p in prepared.values():
+                bench.destroy(p)
+            if log:
+                log(results[-1])
+            continue
+        for p in prepared.values():
+            bench.reset(p)
         t = bench.time(prepared)
         rec = {"id": w["id"], "family": w["family"], "params": w["params"], "k": t["k"], "created": t["created"],
-               "variants": {}}
+               "gate": gt, "variants": {}}
         for name, p in v["programs"].items():
             s = summarize(t["reps"][name])
             rec["variants"][name] = {"launches": p["launches"], "bytes": p["bytes"],

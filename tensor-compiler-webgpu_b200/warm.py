@@ -16,8 +16,12 @@ from .cases import fused_direct_cases
 
 
 def _codes(graph, keep=(), matmul="naive"):
+    """Kernels of a graph fused (as verified, and as a resident program with column sums in their
+    producers) and unfused."""
     f = fuse(graph, keep=list(keep))
+    fk = [f.index[k] for k in keep]
     return {lau.code for lau in cg.lower_fused(f.graph, matmul=matmul)["launches"]} | \
+        {lau.code for lau in cg.lower_fused(f.graph, matmul=matmul, colfuse=True, keep=fk)["launches"]} | \
         {lau.code for lau in cg.lower(graph, matmul=matmul)["launches"]}
 
 
@@ -52,6 +56,8 @@ def standard_sources(full=True):
         f = fuse(gs["graph"], keep=[gs["loss"], *gs["grads"].values()])
         keep = [f.index[i] for i in [gs["loss"], *gs["grads"].values()]]
         codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=keep)["launches"]}
+        codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=keep,
+                                                     colfuse=True)["launches"]}
         ad = _steps.build_adam_graph(c["V"], cfg)
         fa = fuse(ad["graph"], keep=list(ad["outputs"].values()))
         codes |= {lau.code for lau in cg.lower_fused(fa.graph, matmul="tiled")["launches"]}

@@ -138,7 +138,7 @@ def _replay(prog, graph):
 
     for lau in prog.launches:
         members = getattr(lau, "members", [lau])
-        outs = [m.node for m in members]
+        outs = [n for m in members for n in (getattr(m, "nodes", None) or [m.node])]  # two-output launches too
         for m in members:
             for i in m.inputs:
                 if nodes[root(i)].op in ("input", "const"):
