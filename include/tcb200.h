@@ -153,6 +153,54 @@ int tc_plan_free(tc_plan* plan);
 int tc_plan_memory(int n, const uint64_t* bytes, const int32_t* first_use, const int32_t* last_use,
                    uint64_t* offsets, uint64_t* total);
 
+/* ---- lowering from a graph, with no host language in between: lower() (src/gpu/lower.js:68-114),
+ *      lowerFused() (src/fusion/lower-fused.js:32-45) and fusedKernel()
+ *      (src/fusion/codegen-fused.js:357-362).  `graph_json` is the reference's Graph.toJSON form
+ *      ({"nodes": [{op, inputs, attrs, shape}]}, src/ir/graph.js:48-50); with "fused" true it may hold
+ *      the fusion pass's fused nodes (attrs {kind, pattern, body, output}, src/fusion/fuse.js:278-279).
+ *      `opts_json` (NULL = defaults): {"fused": true (lowerFused; false: lower), "matmul": "naive" |
+ *      "tiled" (the tcgen05 3xTF32 GEMM where K >= 32), "sabotage": one of the reference's
+ *      FUSED_SABOTAGE names or null, "fold": false (transposes read only as GEMM operands get no launch),
+ *      "colfuse": false (sums over axis 0 run inside their elementwise producer), "keep": [node ids that
+ *      must exist after the launches]}.  No device is needed.  Each launch's CUDA source, kernel calls
+ *      (grid, block, shared memory, parameters, tensor maps, error word) and scratch are those the
+ *      repository's Python host makes, character for character. ---- */
+typedef struct tc_lowered tc_lowered;
+int tc_lower_json(const char* graph_json, const char* opts_json, tc_lowered** out);
+int tc_lowered_count(tc_lowered* l, int* n);
+/* The launch records as JSON ({"launches": [{node, nodes?, op, kind, pattern, inputs, code, scratch_bytes,
+ * bytes, calls: [{name, grid, block, smem, params, err_offset, out_node, ptr_params, tma}], info}],
+ * "folded": [...]}, the reference's {node, op, kind, pattern, inputs, params, grid, code} record,
+ * src/gpu/lower.js:108-111) into `json` (cap bytes); *needed = its size with the NUL.  json may be NULL. */
+int tc_lowered_json(tc_lowered* l, char* json, uint64_t cap, uint64_t* needed);
+int tc_lowered_free(tc_lowered* l);
+
+/* GpuRunner.run (src/gpu/runtime.js:60-129) of a lowering: a buffer per node (canary-padded when
+ * `canary`), the inputs and constants uploaded, every launch in order, every requested node read back.
+ * inputs[i]: float32 host data of input node i (other entries ignored); values[i]: where node i's value
+ * goes (NULL = not read; values itself may be NULL); canary_intact[i] (optional): 1 when node i's padding
+ * is intact.  Arrays are indexed by node id.  Kernels come from the on-disk cache beside the library
+ * ($TCB_KERNEL_CACHE overrides), compiled by NVRTC on a miss. */
+int tc_lowered_run(tc_ctx* ctx, tc_lowered* l, const float* const* inputs, float* const* values, int canary,
+                   int* canary_intact);
+
+/* The resident program of GpuTrainer / FusedTrainer (src/gpu/trainer.js:13-104,
+ * src/fusion/trainer-fused.js:135-213): inputs, constants, `keep` values and both ends of each
+ * `feedback` pair (from, to: after the launches `from` is copied into `to`) own buffers, every other
+ * value lives in one lifetime-planned arena, a plain reshape shares its source's memory, a launch nothing
+ * kept or fed back depends on is left out; the launches and copies replay from one native plan (one CUDA
+ * graph with `capture`).  The lowering must outlive the program. */
+typedef struct tc_program tc_program;
+int tc_program_create(tc_ctx* ctx, tc_lowered* l, const int32_t* keep, int n_keep, const int32_t* feedback,
+                      int n_feedback, int capture, tc_program** out);
+int tc_program_write(tc_program* p, int node, const float* host, uint64_t count);   /* synchronous */
+int tc_program_read(tc_program* p, int node, float* host, uint64_t count);          /* synchronous */
+int tc_program_run(tc_program* p);                                                   /* asynchronous */
+int tc_program_check(tc_program* p);     /* TC_ERR_TIMEOUT if a launch's bounded wait ran out (syncs) */
+int tc_program_ptr(tc_program* p, int node, uint64_t* dptr);
+int tc_program_launch_count(tc_program* p, int* n);
+int tc_program_free(tc_program* p);
+
 /* ---- allocation-free column sum.  No counterpart in the reference: it exists for
  *      callers that cannot allocate device memory where they need the reduction (inside
  *      a stream capture, under another allocator's fixed budget, or on a path that

@@ -1031,11 +1031,17 @@ def _plain_launch_uncached(op, in_shapes, attrs, matmul):
 _plain_cache = {}
 
 
+_GEMM_ENV = ("TCB_GEMM_FUSED", "TCB_GEMM_FS_REREAD", "TCB_GEMM_BK", "TCB_GEMM_BN")
+
+
 def _plain_launch(graph, node, matmul):
-    """The launch one node gets alone, cached by (op, shapes, attrs, matmul) (src/fusion/lower-fused.js:13-25)."""
+    """The launch one node gets alone, cached by (op, shapes, attrs, matmul) (src/fusion/lower-fused.js:13-25)
+    and by the GEMM tile overrides in the environment, which change a matmul's launch."""
     import json
+    import os
     shapes = [list(graph.nodes[i].shape) for i in node.inputs]
-    key = json.dumps([node.op, shapes, node.attrs, matmul], sort_keys=True)
+    env = [os.environ.get(k) for k in _GEMM_ENV] if node.op == "matmul" else None
+    key = json.dumps([node.op, shapes, node.attrs, matmul, env], sort_keys=True)
     one = _plain_cache.get(key)
     if one is None:
         one = _plain_cache[key] = _plain_launch_uncached(node.op, shapes, node.attrs, matmul)

@@ -112,6 +112,22 @@ _SIGS = {
                         ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "tc_colsum_f32_static": ([ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64],
                              ctypes.c_int),
+    "tc_lower_json": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "tc_lowered_count": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "tc_lowered_json": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "tc_lowered_free": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_lowered_run": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                        ctypes.c_int, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "tc_program_create": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
+                           ctypes.POINTER(ctypes.c_int32), ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)],
+                          ctypes.c_int),
+    "tc_program_write": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
+    "tc_program_read": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64], ctypes.c_int),
+    "tc_program_run": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_program_check": ([ctypes.c_void_p], ctypes.c_int),
+    "tc_program_ptr": ([ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "tc_program_launch_count": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "tc_program_free": ([ctypes.c_void_p], ctypes.c_int),
     "tc_comm_unique_id": ([ctypes.c_char_p], ctypes.c_int),
     "tc_comm_init": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
                       ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),

@@ -230,3 +230,18 @@ def test_multi_instance_modules_compile(cg):
     rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
     for src in (cg.copy_source(4), cg.copy_source(1), cg.split_multi_source()):
         assert rt.compile_check(src) > 0
+
+
+def test_plain_launch_cache_follows_the_gemm_overrides(pkg, monkeypatch):
+    """A one-op matmul lowered under one GEMM override is not reused under another: the cache is keyed by
+    the overrides too (a reference lowering under TCB_GEMM_FUSED=0 must split its operands by passes even
+    after a default lowering of the same shapes)."""
+    import importlib
+    cg = importlib.import_module("tensor-compiler-webgpu_b200.codegen")
+    g = pkg.ir.Graph()
+    g.matmul(g.input("a", [64, 128]), g.input("b", [128, 64]))
+    monkeypatch.delenv("TCB_GEMM_FUSED", raising=False)
+    (a,) = cg.lower(g, matmul="tiled")["launches"]
+    monkeypatch.setenv("TCB_GEMM_FUSED", "0")
+    (b,) = cg.lower(g, matmul="tiled")["launches"]
+    assert a.info["fused_split"] == (True, True) and b.info["fused_split"] == (False, False)
