@@ -176,8 +176,8 @@ def build_workload(name, wl, pkg, cg, rows=None, variant=None, shape=None):
         raise SystemExit(f"unknown workload {name}")
     graph = W["graph"]
     fused = pkg.fuse.fuse(graph, keep=W["keep"])
-    # the resident program's lowering: column sums run inside their elementwise producers
-    lowered = cg.lower_fused(fused.graph, matmul="tiled" if name == "c3" else "naive", colfuse=True,
+    # the resident program's lowering: column sums and elementwise readers run inside their producers
+    lowered = cg.lower_fused(fused.graph, matmul="tiled" if name == "c3" else "naive", colfuse=True, mofuse=True,
                              keep=[fused.index[k] for k in W["keep"]])
     return graph, fused, lowered, inputs, W["keep"], cfg, W
 

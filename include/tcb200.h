@@ -161,8 +161,9 @@ int tc_plan_memory(int n, const uint64_t* bytes, const int32_t* first_use, const
  *      `opts_json` (NULL = defaults): {"fused": true (lowerFused; false: lower), "matmul": "naive" |
  *      "tiled" (the tcgen05 3xTF32 GEMM where K >= 32), "sabotage": one of the reference's
  *      FUSED_SABOTAGE names or null, "fold": false (transposes read only as GEMM operands get no launch),
- *      "colfuse": false (sums over axis 0 run inside their elementwise producer), "keep": [node ids that
- *      must exist after the launches]}.  No device is needed.  Each launch's CUDA source, kernel calls
+ *      "colfuse": false (sums over axis 0 run inside their elementwise producer), "mofuse": false (an
+ *      elementwise reader whose other operands already exist is computed in its elementwise producer's
+ *      pass, both stored), "keep": [node ids that must exist after the launches]}.  No device is needed.  Each launch's CUDA source, kernel calls
  *      (grid, block, shared memory, parameters, tensor maps, error word) and scratch are those the
  *      repository's Python host makes, character for character. ---- */
 typedef struct tc_lowered tc_lowered;

@@ -119,6 +119,15 @@ class Gather:
     def key(self):
         return (self.kind, tuple(self.dims))
 
+    def vec4(self):
+        """A general gather whose innermost run is contiguous (stride 1, a multiple of 4 long) and whose
+        other strides are multiples of 4: 4 consecutive outputs starting at a multiple of 4 read 4
+        consecutive, 16-byte aligned source floats."""
+        if self.kind != "general" or not self.dims:
+            return False
+        d, g = self.dims[-1]
+        return g == 1 and d % 4 == 0 and all(gg % 4 == 0 for _, gg in self.dims[:-1])
+
 
 class Ctx:
     """An index context: the base index, or a gathered index computed from a parent context."""
@@ -255,6 +264,10 @@ class _EwLoads:
             self.fields.append(f"float {name};")
             self.stmts.append(f"r.{name} = tcb::ld1({ptr} + {g.expr(f'({T})i0', T)});")
             ref = f"r.{name}"
+        elif ctx.parent.parent is None and g.vec4():
+            self.fields.append(f"float {name}[W];")
+            self.stmts.append(f"tcb::load<W>(r.{name}, {ptr} + {g.expr(f'({T})i0', T)});")
+            ref = f"r.{name}[l]"
         else:
             self.fields.append(f"float {name}[W];")
             self.per_lane.append(f"r.{name}[l] = tcb::ld1({ptr} + {_chain_index(ctx, f'(({T})i0 + ({T})l)', T)});")
@@ -527,6 +540,7 @@ def _rowwise_source(body, out_id, pattern, sabotage=None):
 #include "tcb/common.cuh"
 #include "tcb/rowwise.cuh"
 extern "C" __global__ void __launch_bounds__({TPR * GROUPS}) tcb_rowwise(const tcb::Args a) {{
+  tcb::grid_dependency_sync();
   __shared__ float red[{GROUPS * nw}];
   float* __restrict__ out = reinterpret_cast<float*>(a.out);
   const int g = threadIdx.x / {TPR};
@@ -1215,6 +1229,141 @@ def _colsum_launch(graph, P, S, write):
     return lau
 
 
+# ------------------------------------------------------------------ one pass, several elementwise outputs
+MO_MAX_OPERANDS = 8
+
+
+def _reads_directly(node, k):
+    """Whether operand slot k of an elementwise launch's node is read only at the output's own index
+    (a plain op reads every operand so; a fused body must use input a<k> only in elementwise ops)."""
+    if node.op != "fused":
+        return True
+    from .fuse import body_of
+    body = body_of(node)
+    nid = next(n.id for n in body.nodes if n.op == "input" and n.attrs["name"] == f"a{k}")
+    return all(n.op in _BIN or n.op in _UN for n in body.nodes if nid in n.inputs)
+
+
+def mo_fusions(graph, keep=(), exclude=()):
+    """Readers computed in their producer's pass: {producer id: reader id}.
+
+    A producer is an elementwise launch (a fused elementwise node or a plain elementwise op) whose value
+    must be stored (another node or the caller reads it); a reader qualifies when it is an elementwise
+    launch of the same shape that reads the producer at its own index, and every other operand it has
+    is a graph input, a constant or a value produced earlier, so the one launch can stand at the
+    producer's place.  Each node takes part in one pair at most; together they read at most 8 operands.
+    With `keep` given, a reader qualifies only if a kept value depends on it (a resident program leaves
+    the other readers out altogether).  `exclude`: nodes another rewrite already owns (fused column
+    sums, folded transposes)."""
+    exclude = set(exclude)
+    live = None
+    if keep:
+        live = set(keep)
+        for n in reversed(graph.nodes):
+            if n.id in live:
+                live.update(n.inputs)
+    consumers = {}
+    for n in graph.nodes:
+        for i in n.inputs:
+            consumers.setdefault(i, []).append(n.id)
+    used, out = set(exclude), {}
+    for P in graph.nodes:
+        if P.id in used or not _elementwise_producer(P):
+            continue
+        for qid in consumers.get(P.id, []):
+            Q = graph.nodes[qid]
+            if qid in used or not _elementwise_producer(Q) or Q.shape != P.shape or (live is not None and qid not in live):
+                continue
+            if any(i != P.id and not (graph.nodes[i].op in ("input", "const") or i < P.id) for i in Q.inputs):
+                continue
+            if not all(_reads_directly(Q, k) for k, i in enumerate(Q.inputs) if i == P.id):
+                continue
+            operands = list(dict.fromkeys(list(P.inputs) + [i for i in Q.inputs if i != P.id]))
+            if len(operands) > MO_MAX_OPERANDS:
+                continue
+            out[P.id] = qid
+            used.update((P.id, qid))
+            break
+    return out
+
+
+def _body_and_output(graph, node):
+    from .fuse import body_of
+    if node.op == "fused":
+        return body_of(node), node.attrs["output"]
+    return _one_op_body(node.op, [graph.nodes[i].shape for i in node.inputs], node.attrs)
+
+
+def _merged_body(graph, P, Q):
+    """One body computing P and its reader Q: operands = P's operands then Q's other ones (first
+    appearance order); Q's reads of P use P's value.  Returns (body, [P's output, Q's output], operands)."""
+    from .ir import Graph
+    operands = list(dict.fromkeys(list(P.inputs) + [i for i in Q.inputs if i != P.id]))
+    g = Graph()
+    slot = {nid: g.input(f"a{k}", graph.nodes[nid].shape) for k, nid in enumerate(operands)}
+    outs = []
+    for node, reads_p in ((P, None), (Q, P.id)):
+        body, out = _body_and_output(graph, node)
+        remap = {}
+        for n in body.nodes:
+            if n.op == "input":
+                src = node.inputs[int(n.attrs["name"][1:])]
+                remap[n.id] = outs[0] if src == reads_p else slot[src]
+            else:
+                remap[n.id] = g.emit(n.op, [remap[i] for i in n.inputs], n.attrs)
+        outs.append(remap[out])
+    return g, outs, operands
+
+
+def _mo_source(body, out_ids, n):
+    """The elementwise-with-several-outputs kernel of a merged body (tcb/elementwise_mo.cuh)."""
+    T = idx_type(n)
+    loads = _EwLoads("W", T)
+    em = Emitter(body, loads.leaf)
+    base = Ctx("i")
+    outs = [em.value(o, base) for o in out_ids]
+    fields = "\n    ".join(loads.fields) or "float unused_;"
+    stmts = "\n    ".join(loads.stmts)
+    lanes = "\n      ".join(loads.per_lane)
+    per_lane = f"#pragma unroll\n    for (int l = 0; l < W; ++l) {{\n      {lanes}\n    }}" if loads.per_lane else ""
+    comp = "\n      ".join(em.lines)
+    stores = "\n      ".join(f"o[{k}][l] = {v};" for k, v in enumerate(outs))
+    return f"""// elementwise, {len(out_ids)} outputs: generated from a body of {len(body.nodes)} nodes, {n} elements
+#include "tcb/common.cuh"
+#define TCB_W 4
+#define TCB_NOUT {len(out_ids)}
+struct Body {{
+  template <int W> struct Regs {{
+    {fields}
+  }};
+  template <int W> __device__ __forceinline__ static void load(const tcb::Args& a, u64 i0, Regs<W>& r) {{
+    {stmts}
+    {per_lane}
+  }}
+  template <int W> __device__ __forceinline__ static void compute(const Regs<W>& r, float (&o)[TCB_NOUT][W]) {{
+#pragma unroll
+    for (int l = 0; l < W; ++l) {{
+      {comp}
+      {stores}
+    }}
+  }}
+}};
+#include "tcb/elementwise_mo.cuh"
+"""
+
+
+def _mo_launch(graph, P, Q):
+    body, out_ids, operands = _merged_body(graph, P, Q)
+    n = size(P.shape)
+    call = KernelCall("tcb_elementwise_mo", grid1d(n), (WG, 1, 1), 0, [n])
+    call.ptr_params = ((1, Q.id),)
+    lau = Launch(P.id, "fused", "fused-multi", "elementwise+reader", operands, _mo_source(body, out_ids, n), [call],
+                 info={"producer": P.id, "reader": Q.id, "outputs": 2})
+    lau.nodes = [P.id, Q.id]
+    lau.bytes = sum(size(graph.nodes[i].shape) * 4 for i in operands) + 2 * n * 4
+    return lau
+
+
 def fused_kernel(node, matmul="naive", sabotage=None):
     """The launch of a fused node (src/fusion/codegen-fused.js:357-362)."""
     from .fuse import body_of
@@ -1233,7 +1382,7 @@ def fused_kernel(node, matmul="naive", sabotage=None):
     raise ValueError(f"no fused kernel kind '{kind}'")
 
 
-def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfuse=False):
+def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfuse=False, mofuse=False):
     """A fused node to its kernel, every other node to its plain launch (src/fusion/lower-fused.js:32-45).
 
     `fold` (resident programs only): transposeLast2 nodes read only as tensor-core GEMM operands get no
@@ -1242,13 +1391,20 @@ def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfu
     `colfuse` (resident programs only): a sum over axis 0 runs in its elementwise producer's launch
     (colsum_fusions); a producer read by nothing else is then never stored.  `keep` names the values
     that must exist after the launches.
+    `mofuse` (resident programs only): an elementwise reader whose other operands already exist is
+    computed in its elementwise producer's launch, both stored (mo_fusions).
     """
     folds = foldable_transposes(graph, matmul, keep) if fold else set()
     cols = colsum_fusions(graph, keep) if colfuse else {}
     producer_of = {p: (sid, w) for sid, (p, w) in cols.items()}
+    mos = mo_fusions(graph, keep, exclude=set(cols) | set(producer_of) | folds) if mofuse else {}
+    readers = set(mos.values())
     launches = []
     for node in graph.nodes:
-        if node.op in ("input", "const") or node.id in folds:
+        if node.op in ("input", "const") or node.id in folds or node.id in readers:
+            continue
+        if node.id in mos:                # a producer computing its reader too
+            launches.append(_mo_launch(graph, node, graph.nodes[mos[node.id]]))
             continue
         if node.id in producer_of:        # the producer of a fused column sum
             sid, write = producer_of[node.id]

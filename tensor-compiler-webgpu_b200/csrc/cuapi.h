@@ -13,7 +13,7 @@
   X(cuDeviceGetName) X(cuDevicePrimaryCtxRelease) X(cuDevicePrimaryCtxRetain) X(cuDeviceTotalMem)         \
   X(cuDriverGetVersion) X(cuEventCreate) X(cuEventDestroy) X(cuEventElapsedTime) X(cuEventQuery)          \
   X(cuEventRecord) X(cuEventSynchronize) X(cuFuncSetAttribute) X(cuGetErrorName) X(cuGraphDestroy)        \
-  X(cuGraphExecDestroy) X(cuGraphInstantiate) X(cuGraphLaunch) X(cuInit) X(cuLaunchKernel) X(cuMemAlloc) \
+  X(cuGraphExecDestroy) X(cuGraphInstantiate) X(cuGraphLaunch) X(cuInit) X(cuLaunchKernel) X(cuLaunchKernelEx) X(cuMemAlloc) \
   X(cuMemFree) X(cuMemFreeHost) X(cuMemHostAlloc) X(cuMemcpyDtoDAsync) X(cuMemcpyDtoHAsync)              \
   X(cuMemcpyHtoDAsync) X(cuMemsetD32Async) X(cuModuleGetFunction) X(cuModuleLoadData) X(cuModuleUnload)  \
   X(cuStreamBeginCapture) X(cuStreamCreate) X(cuStreamDestroy) X(cuStreamEndCapture)                      \

@@ -239,6 +239,16 @@ struct Gather {
     return s + ")";
   }
 
+  // A general gather whose innermost run is contiguous (stride 1, a multiple of 4 long) and whose
+  // other strides are multiples of 4: 4 consecutive outputs from a multiple of 4 read 4 aligned floats.
+  bool vec4() const {
+    if (kind != "general" || dims.empty()) return false;
+    if (dims.back().second != 1 || dims.back().first % 4 != 0) return false;
+    for (size_t k = 0; k + 1 < dims.size(); ++k)
+      if (dims[k].second % 4 != 0) return false;
+    return true;
+  }
+
   std::string key() const {
     std::string s = kind + "[";
     for (auto& d : dims) s += std::to_string(d.first) + ":" + std::to_string(d.second) + ",";
@@ -426,6 +436,10 @@ struct EwLoads {
       fields.push_back("float " + name + ";");
       stmts.push_back("r." + name + " = tcb::ld1(" + ptr + " + " + g.expr("(" + T + ")i0", T) + ");");
       ref = "r." + name;
+    } else if (!ctx->parent->parent && g.vec4()) {
+      fields.push_back("float " + name + "[W];");
+      stmts.push_back("tcb::load<W>(r." + name + ", " + ptr + " + " + g.expr("(" + T + ")i0", T) + ");");
+      ref = "r." + name + "[l]";
     } else {
       fields.push_back("float " + name + "[W];");
       per_lane.push_back("r." + name + "[l] = tcb::ld1(" + ptr + " + " +
@@ -779,6 +793,7 @@ static std::string rowwise_source(const Graph& body, int out_id, const std::stri
       "#include \"tcb/common.cuh\"\n"
       "#include \"tcb/rowwise.cuh\"\n"
       "extern \"C\" __global__ void __launch_bounds__(" + std::to_string(TPR * GROUPS) + ") tcb_rowwise(const tcb::Args a) {\n"
+      "  tcb::grid_dependency_sync();\n"
       "  __shared__ float red[" + std::to_string(GROUPS * nw) + "];\n"
       "  float* __restrict__ out = reinterpret_cast<float*>(a.out);\n"
       "  const int g = threadIdx.x / " + TPRs + ";\n"
@@ -1348,6 +1363,169 @@ static Launch colsum_launch(const Graph& g, const Node& P, const Node& S, bool w
   return l;
 }
 
+// ---------------------------------------------------------------- one pass, several elementwise outputs
+static bool reads_directly(const Node& node, int k) {
+  if (node.op != "fused") return true;
+  const Graph& b = *node.body;
+  int nid = -1;
+  for (auto& n : b.nodes)
+    if (n.op == "input" && n.name == "a" + std::to_string(k)) {
+      nid = n.id;
+      break;
+    }
+  for (auto& n : b.nodes)
+    if (std::find(n.inputs.begin(), n.inputs.end(), nid) != n.inputs.end() && !is_bin(n.op) && !is_un(n.op)) return false;
+  return true;
+}
+
+static std::vector<int> mo_operands(const Node& P, const Node& Q) {
+  std::vector<int> ops;
+  auto add = [&](int i) {
+    if (std::find(ops.begin(), ops.end(), i) == ops.end()) ops.push_back(i);
+  };
+  for (int i : P.inputs) add(i);
+  for (int i : Q.inputs)
+    if (i != P.id) add(i);
+  return ops;
+}
+
+static std::map<int, int> mo_fusions(const Graph& g, const std::set<int>& keep, const std::set<int>& exclude) {
+  std::set<int> live;
+  bool use_live = !keep.empty();
+  if (use_live) {
+    live = keep;
+    for (int i = (int)g.nodes.size() - 1; i >= 0; --i)
+      if (live.count(i))
+        for (int j : g.nodes[i].inputs) live.insert(j);
+  }
+  std::map<int, std::vector<int>> consumers;
+  for (auto& n : g.nodes)
+    for (int i : n.inputs) consumers[i].push_back(n.id);
+  std::set<int> used = exclude;
+  std::map<int, int> out;
+  for (auto& P : g.nodes) {
+    if (used.count(P.id) || !elementwise_producer(P)) continue;
+    for (int qid : consumers[P.id]) {
+      const Node& Q = g.nodes[qid];
+      if (used.count(qid) || !elementwise_producer(Q) || Q.shape != P.shape || (use_live && !live.count(qid))) continue;
+      bool ready = true;
+      for (int i : Q.inputs)
+        if (i != P.id && !(g.nodes[i].op == "input" || g.nodes[i].op == "const" || i < P.id)) ready = false;
+      if (!ready) continue;
+      bool direct = true;
+      for (size_t k = 0; k < Q.inputs.size(); ++k)
+        if (Q.inputs[k] == P.id && !reads_directly(Q, (int)k)) direct = false;
+      if (!direct) continue;
+      if (mo_operands(P, Q).size() > 8) continue;
+      out[P.id] = qid;
+      used.insert(P.id);
+      used.insert(qid);
+      break;
+    }
+  }
+  return out;
+}
+
+static Launch mo_launch(const Graph& g, const Node& P, const Node& Q) {
+  std::vector<int> operands = mo_operands(P, Q);
+  Graph body;
+  std::map<int, int> slot;
+  for (size_t k = 0; k < operands.size(); ++k) {
+    Node in;
+    in.id = (int)k;
+    in.op = "input";
+    in.name = "a" + std::to_string(k);
+    in.shape = g.nodes[operands[k]].shape;
+    in.attr_shape = in.shape;
+    body.nodes.push_back(in);
+    slot[operands[k]] = (int)k;
+  }
+  std::vector<int> outs;
+  const Node* parts[2] = {&P, &Q};
+  for (int w = 0; w < 2; ++w) {
+    const Node& node = *parts[w];
+    std::shared_ptr<Graph> owned;
+    const Graph* b;
+    int out_id;
+    if (node.op == "fused") {
+      b = node.body.get();
+      out_id = node.output;
+    } else {
+      std::vector<std::vector<i64>> shapes;
+      for (int i : node.inputs) shapes.push_back(g.nodes[i].shape);
+      owned = one_op_body(node, shapes, &out_id);
+      b = owned.get();
+    }
+    std::map<int, int> remap;
+    for (auto& n : b->nodes) {
+      if (n.op == "input") {
+        int src = node.inputs[std::stoi(n.name.substr(1))];
+        remap[n.id] = (w == 1 && src == P.id) ? outs[0] : slot[src];
+      } else {
+        Node c = n;
+        c.id = (int)body.nodes.size();
+        for (auto& i : c.inputs) i = remap[i];
+        c.body.reset();
+        body.nodes.push_back(c);
+        remap[n.id] = c.id;
+      }
+    }
+    outs.push_back(remap[out_id]);
+  }
+  i64 n = size_of(P.shape);
+  // the source: the elementwise load plan and emitter over the merged body, one store per output
+  EwLoads loads;
+  loads.T = idx_type(n);
+  Emitter em(body);
+  em.leaf = [&](int k, Ctx* c) { return loads.leaf(k, c); };
+  Ctx base{"i", nullptr, Gather()};
+  std::vector<std::string> vals;
+  for (int o : outs) vals.push_back(em.value(o, &base));
+  std::string fields = loads.fields.empty() ? "float unused_;" : join(loads.fields, "\n    ");
+  std::string per_lane = loads.per_lane.empty()
+                             ? ""
+                             : "#pragma unroll\n    for (int l = 0; l < W; ++l) {\n      " +
+                                   join(loads.per_lane, "\n      ") + "\n    }";
+  std::vector<std::string> stores;
+  for (size_t k = 0; k < vals.size(); ++k) stores.push_back("o[" + std::to_string(k) + "][l] = " + vals[k] + ";");
+  Launch l;
+  l.code = "// elementwise, " + std::to_string(outs.size()) + " outputs: generated from a body of " +
+           std::to_string(body.nodes.size()) + " nodes, " + std::to_string(n) + " elements\n"
+           "#include \"tcb/common.cuh\"\n#define TCB_W 4\n#define TCB_NOUT " + std::to_string(outs.size()) + "\n"
+           "struct Body {\n"
+           "  template <int W> struct Regs {\n"
+           "    " + fields + "\n"
+           "  };\n"
+           "  template <int W> __device__ __forceinline__ static void load(const tcb::Args& a, u64 i0, Regs<W>& r) {\n"
+           "    " + join(loads.stmts, "\n    ") + "\n"
+           "    " + per_lane + "\n"
+           "  }\n"
+           "  template <int W> __device__ __forceinline__ static void compute(const Regs<W>& r, float (&o)[TCB_NOUT][W]) {\n"
+           "#pragma unroll\n"
+           "    for (int l = 0; l < W; ++l) {\n"
+           "      " + join(em.lines, "\n      ") + "\n"
+           "      " + join(stores, "\n      ") + "\n"
+           "    }\n"
+           "  }\n"
+           "};\n"
+           "#include \"tcb/elementwise_mo.cuh\"\n";
+  Call call = make_call("tcb_elementwise_mo", grid1d(n), {WG, 1, 1}, 0, {n});
+  call.ptr_params = {{1, Q.id}};
+  l.calls.push_back(call);
+  l.node = P.id;
+  l.nodes = {P.id, Q.id};
+  l.op = "fused";
+  l.kind = "fused-multi";
+  l.pattern = "elementwise+reader";
+  l.has_pattern = true;
+  l.inputs = operands;
+  l.info = {{"producer", num(P.id)}, {"reader", num(Q.id)}, {"outputs", num(2)}};
+  i64 nb = 0;
+  for (int i : operands) nb += size_of(g.nodes[i].shape) * 4;
+  l.bytes = nb + 2 * n * 4;
+  return l;
+}
+
 // ---------------------------------------------------------------- lower / lowerFused / fusedKernel
 static Launch fused_kernel(const Node& node, const std::string& matmul, const std::string& sabotage) {
   const Graph& body = *node.body;
@@ -1365,7 +1543,7 @@ static Launch fused_kernel(const Node& node, const std::string& matmul, const st
 struct Options {
   bool fused = true;
   std::string matmul = "naive", sabotage;
-  bool fold = false, colfuse = false;
+  bool fold = false, colfuse = false, mofuse = false;
   std::set<int> keep;
 };
 
@@ -1376,8 +1554,21 @@ static void lower_graph(Lowering& L, const Options& o) {
                                                                      : std::map<int, std::pair<int, bool>>();
   std::map<int, std::pair<int, bool>> producer_of;
   for (auto& [sid, pw] : cols) producer_of[pw.first] = {sid, pw.second};
+  std::map<int, int> mos;
+  if (o.fused && o.mofuse) {
+    std::set<int> exclude(folds.begin(), folds.end());
+    for (auto& kv : cols) exclude.insert(kv.first);
+    for (auto& kv : producer_of) exclude.insert(kv.first);
+    mos = mo_fusions(g, o.keep, exclude);
+  }
+  std::set<int> readers;
+  for (auto& kv : mos) readers.insert(kv.second);
   for (auto& node : g.nodes) {
-    if (node.op == "input" || node.op == "const" || folds.count(node.id)) continue;
+    if (node.op == "input" || node.op == "const" || folds.count(node.id) || readers.count(node.id)) continue;
+    if (mos.count(node.id)) {
+      L.launches.push_back(mo_launch(g, node, g.nodes[mos[node.id]]));
+      continue;
+    }
     if (producer_of.count(node.id)) {
       auto [sid, write] = producer_of[node.id];
       if (write) L.launches.push_back(colsum_launch(g, node, g.nodes[sid], true));
@@ -1492,6 +1683,7 @@ int tc_lower_json(const char* graph_json, const char* opts_json, tc_lowered** ou
         if (x->is_string()) o.sabotage = x->as_string();
       if (auto* x = v.find("fold")) o.fold = x->truthy();
       if (auto* x = v.find("colfuse")) o.colfuse = x->truthy();
+      if (auto* x = v.find("mofuse")) o.mofuse = x->truthy();
       if (auto* x = v.find("keep"))
         for (auto& k : x->arr) o.keep.insert((int)k.as_int());
     }

@@ -639,8 +639,11 @@ struct tc_plan {
     tc_args args = {};
     std::shared_ptr<TmaBlock> tma;
     uint64_t dst = 0, src = 0, bytes = 0;
+    bool waits = false;   // a template kernel: it waits for its predecessor itself (grid_dependency_sync)
   };
   std::vector<Entry> entries;
+  // Programmatic dependent launch between consecutive template kernels ($TCB_PDL=0 turns it off).
+  bool pdl = true;
   CUgraph graph = nullptr;
   CUgraphExec exec = nullptr;
   CUstream captured_on = nullptr;
@@ -652,6 +655,8 @@ int tc_plan_create(tc_ctx* ctx, tc_plan** out) {
   if (!ctx || !out) return fail(TC_ERR_INVALID, "null argument");
   *out = new tc_plan();
   (*out)->ctx = ctx;
+  const char* e = getenv("TCB_PDL");
+  (*out)->pdl = !(e && e[0] == '0');
   return TC_OK;
 }
 
@@ -665,6 +670,7 @@ static int plan_add(tc_plan* plan, tc_module* mod, const char* kernel, const uin
   if (int s = get_fn(mod, kernel, &e.fn)) return s;
   if (int s = prepare_smem(e.fn, smem)) return s;
   e.kind = tma ? 1 : 0;
+  e.waits = strncmp(kernel, "tcb_", 4) == 0;
   for (int i = 0; i < 3; i++) { e.grid[i] = grid[i]; e.block[i] = block[i]; }
   e.smem = smem;
   e.args = *args;
@@ -699,19 +705,42 @@ int tc_plan_add_copy(tc_plan* plan, uint64_t dst, uint64_t src, uint64_t bytes) 
   return TC_OK;
 }
 
+// A template kernel that follows another kernel of the plan is launched with programmatic stream
+// serialization: it may be scheduled while its predecessor drains, and waits for it (complete, writes
+// visible) before touching memory.  A copy, a kernel that is not a template's, or the first entry keeps
+// the full ordering.
 static int plan_issue(tc_plan* plan) {
   CUstream st = plan->ctx->stream;
+  bool prev_kernel = false;
   for (auto& e : plan->entries) {
     if (e.kind == 2) {
       if (e.bytes) CU_TRY(CU(cuMemcpyDtoDAsync)((CUdeviceptr)e.dst, (CUdeviceptr)e.src, e.bytes, st));
+      prev_kernel = false;
       continue;
     }
     void* params[1];
     tc_args a = e.args;
     if (e.kind == 1) params[0] = e.tma.get();
     else params[0] = &a;
-    CU_TRY(CU(cuLaunchKernel)(e.fn, e.grid[0], e.grid[1], e.grid[2], e.block[0], e.block[1], e.block[2], e.smem, st,
-                          params, nullptr));
+    if (plan->pdl && e.waits && prev_kernel) {
+      CUlaunchAttribute attr[1];
+      memset(attr, 0, sizeof attr);
+      attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+      attr[0].value.programmaticStreamSerializationAllowed = 1;
+      CUlaunchConfig cfg;
+      memset(&cfg, 0, sizeof cfg);
+      cfg.gridDimX = e.grid[0]; cfg.gridDimY = e.grid[1]; cfg.gridDimZ = e.grid[2];
+      cfg.blockDimX = e.block[0]; cfg.blockDimY = e.block[1]; cfg.blockDimZ = e.block[2];
+      cfg.sharedMemBytes = e.smem;
+      cfg.hStream = st;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      CU_TRY(CU(cuLaunchKernelEx)(&cfg, e.fn, params, nullptr));
+    } else {
+      CU_TRY(CU(cuLaunchKernel)(e.fn, e.grid[0], e.grid[1], e.grid[2], e.block[0], e.block[1], e.block[2], e.smem, st,
+                            params, nullptr));
+    }
+    prev_kernel = true;
   }
   return TC_OK;
 }

@@ -21,6 +21,7 @@
 #include "tcb/reduce.cuh"
 
 extern "C" __global__ void __launch_bounds__(256) tcb_ew_colsum(const tcb::Args a) {
+  tcb::grid_dependency_sync();
   constexpr int W = TCB_W;
   constexpr u64 R = (u64)TCB_N, C = (u64)TCB_INNER, groups = C / W;
   constexpr u64 chunk = (R + TCB_SPLIT - 1) / TCB_SPLIT;

@@ -40,6 +40,16 @@ __device__ __forceinline__ float op_max(float acc, float v) { return v > acc ? v
 
 __device__ __forceinline__ float bits(u32 b) { return __uint_as_float(b); }
 
+// Programmatic dependent launch.  A kernel replayed from a plan may be scheduled while the kernel before
+// it is still draining (the launch carries the programmatic-serialization attribute); it waits here,
+// before it touches any memory, until that kernel has completed and its writes are visible, then lets
+// the kernel after it be scheduled in turn.  Launched without the attribute, both are no-ops.  Every
+// kernel of the library's templates calls this first.
+__device__ __forceinline__ void grid_dependency_sync() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Read-only loads (ld.global.nc); W consecutive floats from a 4W-byte aligned address.
 template <int W>
 __device__ __forceinline__ void load(float (&r)[W], const float* p) {

@@ -54,10 +54,11 @@ __device__ __forceinline__ void elementwise_run(const tcb::Args& a) {
 }
 }  // namespace tcb
 
-extern "C" __global__ void __launch_bounds__(256) tcb_elementwise(const tcb::Args a) { tcb::elementwise_run(a); }
+extern "C" __global__ void __launch_bounds__(256) tcb_elementwise(const tcb::Args a) { tcb::grid_dependency_sync(); tcb::elementwise_run(a); }
 
 // Several launches of this same body over different buffers in one launch (a resident program batches
 // small independent ones): a.scratch holds a device table of argument blocks, blockIdx.y picks one.
 extern "C" __global__ void __launch_bounds__(256) tcb_elementwise_multi(const tcb::Args a) {
+  tcb::grid_dependency_sync();
   tcb::elementwise_run(reinterpret_cast<const tcb::Args*>(a.scratch)[blockIdx.y]);
 }

@@ -283,6 +283,7 @@ __device__ __forceinline__ void split_cols(const float* __restrict__ src, float*
 // A -> A_hi, A_lo [batch, M, Kp] (scratch), zero beyond K.  It runs first in every tensor-core
 // launch, so it also clears that launch's error word (p[15]) in the reused scratch.
 extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a) {
+  tcb::grid_dependency_sync();
   if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && a.p[15]) tcb::clear_ctrl(a);
   float* hi = reinterpret_cast<float*>(a.scratch);
   float* lo = hi + (u64)TCB_BATCH * TCB_M * TCB_KP;
@@ -296,6 +297,7 @@ extern "C" __global__ void __launch_bounds__(256) tcb_split_a(const tcb::Args a)
 
 // B [batch, K, N] -> B_hi^T, B_lo^T [batch, N, Kp] so both operands are K-major.
 extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a) {
+  tcb::grid_dependency_sync();
   float* hi = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(a.scratch) + TCB_SPLIT_B_OFFSET);
   float* lo = hi + (u64)TCB_BATCH * TCB_N * TCB_KP;
   const float* src = reinterpret_cast<const float*>(a.in[TCB_IB]);
@@ -309,6 +311,7 @@ extern "C" __global__ void __launch_bounds__(256) tcb_split_b(const tcb::Args a)
 // With A split in the kernel there is no tcb_split_a: this one-block launch, first in the tensor-core
 // launch, clears its error word (p[15]) and the tail units' arrival counters instead.
 extern "C" __global__ void __launch_bounds__(128) tcb_gemm_prep(const tcb::Args a) {
+  tcb::grid_dependency_sync();
   if (a.p[15]) tcb::clear_ctrl(a);
 }
 
@@ -321,6 +324,7 @@ extern "C" __global__ void __launch_bounds__(128) tcb_gemm_prep(const tcb::Args 
 extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192, 1)
     tcb_gemm_tc(const __grid_constant__ tcb::GemmParams P) {
   using namespace tcb;
+  grid_dependency_sync();
   using S = GemmShape;
   constexpr int BN = TCB_BN, STAGES = TCB_STAGES;
   constexpr bool FA = TCB_FS_A != 0, FB = TCB_FS_B != 0, FS = FA || FB;
@@ -665,6 +669,7 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
 
 // Split-K: out = Epi(sum over splits s = 0.. of partial[s]), in split order (deterministic).
 extern "C" __global__ void __launch_bounds__(256) tcb_splitk_finish(const tcb::Args a) {
+  tcb::grid_dependency_sync();
 #if TCB_SPLITK > 1
   const float* __restrict__ part = reinterpret_cast<const float*>(a.scratch) + TCB_PART_OFFSET / 4;
   float* __restrict__ out = reinterpret_cast<float*>(a.out);

@@ -20,6 +20,7 @@ constexpr int MM_BM = 128, MM_BN = 128, MM_BK = 8;
 
 extern "C" __global__ void __launch_bounds__(256) tcb_matmul(const tcb::Args a) {
   using namespace tcb;
+  grid_dependency_sync();
   __shared__ __align__(16) float As[2][MM_BK][MM_BM];
   __shared__ __align__(16) float Bs[2][MM_BK][MM_BN];
   constexpr u64 M = TCB_M, N = TCB_N, K = TCB_K;

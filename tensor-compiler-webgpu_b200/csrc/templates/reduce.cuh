@@ -18,6 +18,7 @@ __device__ __forceinline__ float red_comb(float acc, float v) { return TCB_IS_MA
 }  // namespace tcb
 
 extern "C" __global__ void __launch_bounds__(256) tcb_reduce_rows(const tcb::Args a) {
+  tcb::grid_dependency_sync();
   const float* __restrict__ x = reinterpret_cast<const float*>(a.in[0]);
   float* __restrict__ out = reinterpret_cast<float*>(a.out);
   const u64 warp = ((u64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -43,6 +44,7 @@ extern "C" __global__ void __launch_bounds__(256) tcb_reduce_rows(const tcb::Arg
 }
 
 extern "C" __global__ void __launch_bounds__(256) tcb_reduce_cols(const tcb::Args a) {
+  tcb::grid_dependency_sync();
   const float* __restrict__ x = reinterpret_cast<const float*>(a.in[0]);
   float* __restrict__ dst = TCB_SPLIT > 1 ? reinterpret_cast<float*>(a.scratch) : reinterpret_cast<float*>(a.out);
   constexpr u64 outs = (u64)TCB_OUTER * (u64)TCB_INNER;
@@ -70,6 +72,7 @@ extern "C" __global__ void __launch_bounds__(256) tcb_reduce_cols(const tcb::Arg
 // coalesced 128-byte row); its 8 warps take the chunks s = w, w + 8, ... in order, and the 8 warp
 // results are combined in warp order -- a fixed order for every output, whatever the launch.
 extern "C" __global__ void __launch_bounds__(256) tcb_reduce_finish(const tcb::Args a) {
+  tcb::grid_dependency_sync();
   const float* __restrict__ part = reinterpret_cast<const float*>(a.scratch);
   float* __restrict__ out = reinterpret_cast<float*>(a.out);
   constexpr u64 outs = (u64)TCB_OUTER * (u64)TCB_INNER;

@@ -24,6 +24,7 @@ __device__ __forceinline__ float split_rna(float x) {
 
 extern "C" __global__ void __launch_bounds__(256) tcb_split_multi(const tcb::Args a) {
   using namespace tcb;
+  grid_dependency_sync();
   const SplitJob j = reinterpret_cast<const SplitJob*>(a.scratch)[blockIdx.y];
   const float* __restrict__ src = reinterpret_cast<const float*>(j.src);
   float* __restrict__ hi = reinterpret_cast<float*>(j.hi);

@@ -67,9 +67,10 @@ class DPTrainer:
     """The transformer training step, data parallel.  `batch_local` sequences per rank."""
 
     def __init__(self, runner, V, batch_local, cfg, params, state=None, comm=None, opt=_steps.ADAM_3B,
-                 matmul="tiled", capture=True, batch=True, colfuse=True):
+                 matmul="tiled", capture=True, batch=True, colfuse=True, mofuse=True):
         """`colfuse`: every bias gradient (a sum over axis 0) runs inside its elementwise producer's
-        launch (codegen.colsum_fusions); values are bitwise those of the separate launches."""
+        launch (codegen.colsum_fusions); `mofuse`: an elementwise reader runs in its producer's pass
+        (codegen.mo_fusions).  Values are bitwise those of the separate launches either way."""
         self.runner, self.comm = runner, comm
         gs = _steps.build_grad3b(V, batch_local, cfg)
         ad = _steps.build_adam_graph(V, cfg, opt)
@@ -95,7 +96,8 @@ class DPTrainer:
         # a gradient the graph gives as a constant zero (no dependence) is still written by its launch
         for gid, off in zip(grad_ids, offs):
             place_g[gid] = self.flat.ptr + off
-        lowered_g = lower_fused(fg.graph, matmul=matmul, fold=True, keep=[self.loss_id, *grad_ids], colfuse=colfuse)
+        lowered_g = lower_fused(fg.graph, matmul=matmul, fold=True, keep=[self.loss_id, *grad_ids], colfuse=colfuse,
+                                mofuse=mofuse)
         self.lowered_g = lowered_g
         self.grad_prog = rt.Program(runner, fg.graph, lowered_g, keep=[self.loss_id], place=place_g, batch=batch)
         fa = fuse(ad["graph"], keep=list(ad["outputs"].values()))

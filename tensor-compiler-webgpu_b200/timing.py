@@ -339,6 +339,7 @@ def _ceiling_source(mode, width):
     return f"""// {mode} ceiling, {width}
 #include "tcb/common.cuh"
 extern "C" __global__ void __launch_bounds__(256) tcb_ceiling(const tcb::Args a) {{
+  tcb::grid_dependency_sync();
   const {T}* __restrict__ src = reinterpret_cast<const {T}*>(a.in[0]);
   {T}* __restrict__ dst = reinterpret_cast<{T}*>(a.out);
   (void)dst;

@@ -22,6 +22,7 @@ def _codes(graph, keep=(), matmul="naive"):
     fk = [f.index[k] for k in keep]
     return {lau.code for lau in cg.lower_fused(f.graph, matmul=matmul)["launches"]} | \
         {lau.code for lau in cg.lower_fused(f.graph, matmul=matmul, colfuse=True, keep=fk)["launches"]} | \
+        {lau.code for lau in cg.lower_fused(f.graph, matmul=matmul, colfuse=True, mofuse=True, keep=fk)["launches"]} | \
         {lau.code for lau in cg.lower(graph, matmul=matmul)["launches"]}
 
 
@@ -58,6 +59,8 @@ def standard_sources(full=True):
         codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=keep)["launches"]}
         codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=keep,
                                                      colfuse=True)["launches"]}
+        codes |= {lau.code for lau in cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=keep,
+                                                     colfuse=True, mofuse=True)["launches"]}
         ad = _steps.build_adam_graph(c["V"], cfg)
         fa = fuse(ad["graph"], keep=list(ad["outputs"].values()))
         codes |= {lau.code for lau in cg.lower_fused(fa.graph, matmul="tiled")["launches"]}

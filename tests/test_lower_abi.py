@@ -6,7 +6,7 @@ records must be the Python host's, field for field: every kernel's CUDA source c
 its calls (grid, block, shared memory, parameters, tensor maps, error word, second outputs), scratch,
 algorithmic bytes and plan details -- over lower() and lowerFused() of the BASELINE workloads, the
 reference's 100 direct cases (each value sabotage too), its 146 golden cases, the transformer's step with
-transposes folded and column sums fused, and a sample of the differential-fuzz corpus, on both matmul
+transposes folded, column sums fused and readers computed in their producers' pass, and a sample of the differential-fuzz corpus, on both matmul
 paths.  The GPU test (tests/test_gpu_lower_abi.py) then runs lowerings made this way.
 """
 import ctypes
@@ -83,6 +83,8 @@ def test_baseline_workloads_lower_identically(pkg, mods):
         keep = [f.index[k] for k in W["keep"]]
         n += _compare(lib, cg, f.graph)
         n += _compare(lib, cg, f.graph, colfuse=True, keep=keep)
+        n += _compare(lib, cg, f.graph, colfuse=True, mofuse=True, keep=keep)
+        n += _compare(lib, cg, f.graph, mofuse=True)
         n += _compare(lib, cg, W["graph"], fused=False)
     for M, K, N in (*wl.C3_SHAPES, (256, 4096, 128), (130, 1024, 96), (2432, 128, 2048), (5120, 256, 1024), (64, 16, 8)):
         for act in ("relu", "tanh"):
@@ -117,6 +119,7 @@ def test_transformer_step_lowers_identically(pkg, mods):
         f = pkg.fuse.fuse(gs["graph"], keep=k0)
         keep = [f.index[i] for i in k0]
         assert _compare(lib, cg, f.graph, matmul="tiled", fold=True, keep=keep, colfuse=True) > 100
+        assert _compare(lib, cg, f.graph, matmul="tiled", fold=True, keep=keep, colfuse=True, mofuse=True) > 100
         _compare(lib, cg, f.graph, matmul="tiled", fold=True, keep=keep)
         _compare(lib, cg, f.graph, matmul="tiled")
         ad = s.build_adam_graph(c["V"], cfg)
@@ -148,6 +151,7 @@ def test_direct_and_golden_cases_lower_identically(pkg, mods):
             _compare(lib, cg, f.graph, matmul=mm)
             _compare(lib, cg, f.graph, matmul=mm, colfuse=True, keep=fk)
             _compare(lib, cg, f.graph, matmul=mm, fold=True, keep=fk)
+            _compare(lib, cg, f.graph, matmul=mm, fold=True, colfuse=True, mofuse=True, keep=fk)
             _compare(lib, cg, G.graph, fused=False, matmul=mm)
 
 
@@ -160,8 +164,10 @@ def test_fuzz_corpus_sample_lowers_identically(pkg, mods):
         G = autodiff.grad(p.graph, p.outputs, [n.id for n in p.graph.inputs()])
         for g, keep in ((p.graph, list(p.outputs)), (G.graph, list(p.outputs) + list(G.grads))):
             f = pkg.fuse.fuse(g, keep=keep)
+            fk = [f.index[k] for k in keep]
             for mm in ("naive", "tiled"):
                 _compare(lib, cg, f.graph, matmul=mm)
+                _compare(lib, cg, f.graph, matmul=mm, colfuse=True, mofuse=True, keep=fk)
                 _compare(lib, cg, g, fused=False, matmul=mm)
 
 
