@@ -3,8 +3,11 @@
 One JSON line.  Its headline (`value`) is BASELINE.json configs[1] (C2): the fused elementwise chain on
 fp32 [8192, 8192], forward + autodiff backward, as the fused launch list the fusion pass gives.  A step =
 every launch of that list once, inputs resident in HBM (each operand is 256 MiB, twice the 126 MB L2, so
-no flush is needed between steps).  value = algorithmic bytes per step (amendment 33: each distinct
-operand once at its own size, plus the output, summed over launches) / device time, summed over ranks.
+no flush is needed between steps).  value = algorithmic bytes per step / device time, summed over ranks,
+the bytes counted over the reference fused plan's launches (amendment 33: each distinct operand once at
+its own size, plus the output) -- the same unit the reference arm counts.  The resident program moves
+fewer bytes than that plan (column sums and elementwise readers run in their producers' passes, unread
+launches are left out); `config.moved_gbs` is the bandwidth of the bytes it does move.
 
 The rest of the metric rides in `records`, each with its own roofline, clocks, end-to-end figure and
 (rank 0, one GPU) CPU baseline:
@@ -339,7 +342,11 @@ def graph_record(args, name, runner, world, rank, local, variant=None, shape=Non
     outs = [fused.index[k] for k in dict.fromkeys(keep)]
     prog = rt.Program(runner, fused.graph, lowered, keep=outs)
     launches = prog.launches   # the launches the step runs (a launch no output depends on is left out)
-    step_bytes = sum(l.bytes for l in launches)
+    moved_bytes = sum(l.bytes for l in launches)
+    # the unit of work: the reference fused plan's algorithmic bytes (amendment 33 over the launches the
+    # reference's lowerFused gives), as the reference arm and the CPU baseline count it; this program moves
+    # fewer (column sums and readers in their producers' passes, unread launches left out)
+    step_bytes = sum(l.bytes for l in cg.lower_fused(fused.graph, matmul="tiled" if name == "c3" else "naive")["launches"])
     name_of = {n.id: n.attrs["name"] for n in fused.graph.nodes if n.op == "input"}
     for nid, nm in name_of.items():
         prog.write(nid, inputs[nm])
@@ -448,7 +455,11 @@ def graph_record(args, name, runner, world, rank, local, variant=None, shape=Non
         "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (mulberry32 seed 0, Box-Muller normals)",
         "config": {**cfg, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
-                   "bytes_per_step": step_bytes, "launches_per_step": len(launches)},
+                   "bytes_per_step": step_bytes, "launches_per_step": len(launches),
+                   "units": "the reference fused plan's algorithmic bytes per step (amendment 33), as the "
+                            "reference arm counts them" if not tensor else "useful matmul flops per step",
+                   "bytes_moved_per_step": moved_bytes,
+                   "moved_gbs": round(world * moved_bytes / (ms_step / 1e3) / 1e9, 1)},
         "roofline": roof,
         "e2e": {"value": round(e2e_value, 2), "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 3), "steps": ke, "ceiling": ceil,
