@@ -708,6 +708,16 @@ def main():
             dist.destroy_process_group()
 
 
+def _collective(tr, world):
+    if world == 1:
+        return "none (1 rank)"
+    if tr.buckets == 1:
+        return f"one NCCL sum-allreduce of the flat gradient buffer ({tr.flat_floats * 4} bytes) after the backward"
+    return (f"{len(tr.bucket_spans)} NCCL sum-allreduces of the flat gradient buffer's buckets "
+            f"({[hi - lo for lo, hi in tr.bucket_spans]} bytes), each issued on a collective stream as soon as "
+            f"the backward has written it, overlapping the rest of the backward")
+
+
 def c5_record(args, runner, world, rank, local):
     """C5: the decoder transformer's training step, data parallel over the batch (tokens/s): every rank
     runs the gradient program on its shard, the library's NCCL communicator sums the gradients (one
@@ -767,8 +777,7 @@ def c5_record(args, runner, world, rank, local):
         "dtype": "f32", "data": "synthetic tokens uniform 0..64 (mulberry32 seed 0), weights N(0,0.02)",
         "config": {"workload": "C5 decoder transformer train step (fwd+bwd+Adam)", "V": V, "d": cfg["d"],
                    "L": cfg["L"], "H": cfg["H"], "ff": cfg["ff"], "seq_len": T, "global_batch": B,
-                   "parallelism": f"dp{world}", "collective": "one NCCL sum-allreduce of the flat gradient buffer "
-                   f"({tr.flat_floats * 4} bytes) per step (tc_allreduce_f32)" if world > 1 else "none (1 rank)",
+                   "parallelism": f"dp{world}", "collective": _collective(tr, world),
                    "launches_per_step": tr.kernel_launches,
                    "arena_bytes": tr.grad_prog.arena_bytes + tr.adam_prog.arena_bytes,
                    "l2": "activations > L2 (each [B*T, ff] tensor 512 MiB at one rank)"},

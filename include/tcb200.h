@@ -142,9 +142,16 @@ int tc_plan_add_launch_tma(tc_plan* plan, tc_module* mod, const char* kernel, co
                            const uint32_t block[3], uint32_t smem_bytes, int n_maps, const uint64_t* map_desc,
                            const tc_args* args);
 int tc_plan_add_copy(tc_plan* plan, uint64_t dst, uint64_t src, uint64_t bytes);
+/* A sum-allreduce of `count` floats at `buf` (scaled by `scale`) over `comm`, ordered after every entry
+ * before it but run on the plan's own high-priority collective stream, so the entries after it compute
+ * while it runs: the data-parallel step's gradient buckets, each reduced as soon as the backward has
+ * written it.  The reference has no collective; this replaces the one allreduce that otherwise runs
+ * between the gradient and Adam programs.  The plan's end waits for every collective it issued. */
+int tc_plan_add_allreduce(tc_plan* plan, tc_comm* comm, uint64_t buf, uint64_t count, float scale);
 int tc_plan_run(tc_plan* plan);                    /* every entry, in order, on the context's stream */
 int tc_plan_run_on(tc_plan* plan, uint64_t stream);  /* the same on another stream of the context */
-int tc_plan_capture(tc_plan* plan);                /* later runs replay one CUDA graph */
+int tc_plan_capture(tc_plan* plan);                /* later runs replay one CUDA graph per segment between
+                                                      allreduce entries; the collectives stay outside them */
 int tc_plan_launch_count(tc_plan* plan, int* n);
 int tc_plan_free(tc_plan* plan);
 
@@ -224,6 +231,8 @@ int tc_comm_unique_id(char id[128]);
 int tc_comm_init(tc_ctx* ctx, int rank, int world, const char id[128], int timeout_ms, tc_comm** out);
 /* Sum-allreduce `count` floats in place, then scale by `scale` (fused into the same stream). */
 int tc_allreduce_f32(tc_comm* comm, uint64_t buf, uint64_t count, float scale);
+/* The same on `stream` (a CUstream of the communicator's context; 0 = the context's stream). */
+int tc_allreduce_f32_on(tc_comm* comm, uint64_t buf, uint64_t count, float scale, uint64_t stream);
 int tc_comm_wait(tc_comm* comm, int timeout_ms);   /* bounded; aborts the communicator on timeout */
 int tc_comm_abort(tc_comm* comm);
 int tc_comm_destroy(tc_comm* comm);

@@ -156,12 +156,12 @@ int tc_comm_init(tc_ctx* ctx, int rank, int world, const char id[128], int timeo
   return TC_OK;
 }
 
-int tc_allreduce_f32(tc_comm* c, uint64_t buf, uint64_t count, float scale) {
+int tc_allreduce_f32_on(tc_comm* c, uint64_t buf, uint64_t count, float scale, uint64_t stream) {
   if (!c) return fail(TC_ERR_INVALID, "null communicator");
   if (c->aborted) return fail(TC_ERR_NCCL, "communicator was aborted");
   Nccl* n = nccl();
   if (CU(cuCtxSetCurrent)(tcb_detail::ctx_of(c->ctx)) != CUDA_SUCCESS) return fail(TC_ERR_CUDA, "cuCtxSetCurrent");
-  cudaStream_t st = (cudaStream_t)tcb_detail::stream_of(c->ctx);
+  cudaStream_t st = stream ? (cudaStream_t)(uintptr_t)stream : (cudaStream_t)tcb_detail::stream_of(c->ctx);
   ncclRedOp_t op = ncclSum;
   bool custom = false;
   if (scale != 1.0f) {
@@ -176,6 +176,10 @@ int tc_allreduce_f32(tc_comm* c, uint64_t buf, uint64_t count, float scale) {
   if (custom && n->RedOpDestroy) n->RedOpDestroy(op, c->comm);
   if (r != ncclSuccess) return fail(TC_ERR_NCCL, "ncclAllReduce: %s", n->GetErrorString(r));
   return TC_OK;
+}
+
+int tc_allreduce_f32(tc_comm* c, uint64_t buf, uint64_t count, float scale) {
+  return tc_allreduce_f32_on(c, buf, count, scale, 0);
 }
 
 int tc_comm_wait(tc_comm* c, int timeout_ms) {

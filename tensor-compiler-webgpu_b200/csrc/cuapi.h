@@ -17,7 +17,8 @@
   X(cuMemFree) X(cuMemFreeHost) X(cuMemHostAlloc) X(cuMemcpyDtoDAsync) X(cuMemcpyDtoHAsync)              \
   X(cuMemcpyHtoDAsync) X(cuMemsetD32Async) X(cuModuleGetFunction) X(cuModuleLoadData) X(cuModuleUnload)  \
   X(cuStreamBeginCapture) X(cuStreamCreate) X(cuStreamDestroy) X(cuStreamEndCapture)                      \
-  X(cuStreamSynchronize) X(cuTensorMapEncodeTiled) X(cuStreamWaitEvent)
+  X(cuStreamSynchronize) X(cuTensorMapEncodeTiled) X(cuStreamWaitEvent) X(cuStreamCreateWithPriority)     \
+  X(cuCtxGetStreamPriorityRange)
 
 #define TCB_STR2(x) #x
 #define TCB_STR(x) TCB_STR2(x)

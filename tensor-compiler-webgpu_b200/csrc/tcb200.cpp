@@ -633,20 +633,29 @@ int tc_event_destroy(uint64_t ev) {
 struct tc_plan {
   tc_ctx* ctx = nullptr;
   struct Entry {
-    int kind = 0;  // 0 launch, 1 launch with tensor maps, 2 copy
+    int kind = 0;  // 0 launch, 1 launch with tensor maps, 2 copy, 3 sum-allreduce on the collective stream
     CUfunction fn = nullptr;
     uint32_t grid[3] = {1, 1, 1}, block[3] = {1, 1, 1}, smem = 0;
     tc_args args = {};
     std::shared_ptr<TmaBlock> tma;
-    uint64_t dst = 0, src = 0, bytes = 0;
+    uint64_t dst = 0, src = 0, bytes = 0;   // a copy; an allreduce: dst = buffer, bytes = float count
     bool waits = false;   // a template kernel: it waits for its predecessor itself (grid_dependency_sync)
+    tc_comm* comm = nullptr;
+    float scale = 1.0f;
+    CUevent ready = nullptr;  // an allreduce: recorded on the plan's stream, waited for by the collective stream
   };
   std::vector<Entry> entries;
   // Programmatic dependent launch between consecutive template kernels ($TCB_PDL=0 turns it off).
   bool pdl = true;
-  CUgraph graph = nullptr;
-  CUgraphExec exec = nullptr;
-  CUstream captured_on = nullptr;
+  // Captured form: one graph per segment between allreduce entries (a collective is never captured; it is
+  // enqueued between the segments' graph launches).  Empty segments have none.
+  bool captured = false;
+  std::vector<CUgraph> graphs;
+  std::vector<CUgraphExec> execs;
+  // The collective stream (highest priority, created with the first allreduce entry) and the event the
+  // plan's stream waits for at the plan's end, after its last collective.
+  CUstream coll = nullptr;
+  CUevent joined = nullptr;
 };
 
 extern "C" {
@@ -663,7 +672,7 @@ int tc_plan_create(tc_ctx* ctx, tc_plan** out) {
 static int plan_add(tc_plan* plan, tc_module* mod, const char* kernel, const uint32_t grid[3], const uint32_t block[3],
                     uint32_t smem, int n_maps, const uint64_t* map_desc, const tc_args* args, bool tma) {
   if (!plan || !mod || !kernel || !args) return fail(TC_ERR_INVALID, "null argument");
-  if (plan->exec) return fail(TC_ERR_INVALID, "plan already captured");
+  if (plan->captured) return fail(TC_ERR_INVALID, "plan already captured");
   if (int s = bind(plan->ctx)) return s;
   if (int s = check_geometry(plan->ctx, grid, block, smem)) return s;
   tc_plan::Entry e;
@@ -697,7 +706,7 @@ int tc_plan_add_launch_tma(tc_plan* plan, tc_module* mod, const char* kernel, co
 
 int tc_plan_add_copy(tc_plan* plan, uint64_t dst, uint64_t src, uint64_t bytes) {
   if (!plan) return fail(TC_ERR_INVALID, "null plan");
-  if (plan->exec) return fail(TC_ERR_INVALID, "plan already captured");
+  if (plan->captured) return fail(TC_ERR_INVALID, "plan already captured");
   tc_plan::Entry e;
   e.kind = 2;
   e.dst = dst; e.src = src; e.bytes = bytes;
@@ -705,14 +714,35 @@ int tc_plan_add_copy(tc_plan* plan, uint64_t dst, uint64_t src, uint64_t bytes) 
   return TC_OK;
 }
 
-// A template kernel that follows another kernel of the plan is launched with programmatic stream
-// serialization: it may be scheduled while its predecessor drains, and waits for it (complete, writes
-// visible) before touching memory.  A copy, a kernel that is not a template's, or the first entry keeps
-// the full ordering.
-static int plan_issue(tc_plan* plan) {
-  CUstream st = plan->ctx->stream;
+int tc_plan_add_allreduce(tc_plan* plan, tc_comm* comm, uint64_t buf, uint64_t count, float scale) {
+  if (!plan || !comm) return fail(TC_ERR_INVALID, "null argument");
+  if (plan->captured) return fail(TC_ERR_INVALID, "plan already captured");
+  if (int s = bind(plan->ctx)) return s;
+  if (!plan->coll) {
+    int least = 0, greatest = 0;
+    CU_TRY(CU(cuCtxGetStreamPriorityRange)(&least, &greatest));
+    CU_TRY(CU(cuStreamCreateWithPriority)(&plan->coll, CU_STREAM_NON_BLOCKING, greatest));
+    CU_TRY(CU(cuEventCreate)(&plan->joined, CU_EVENT_DISABLE_TIMING));
+  }
+  tc_plan::Entry e;
+  e.kind = 3;
+  e.comm = comm;
+  e.dst = buf;
+  e.bytes = count;
+  e.scale = scale;
+  CU_TRY(CU(cuEventCreate)(&e.ready, CU_EVENT_DISABLE_TIMING));
+  plan->entries.push_back(e);
+  return TC_OK;
+}
+
+// Entries [b, end) of one segment (kernels and copies) on `st`.  A template kernel that follows another
+// kernel of the segment is launched with programmatic stream serialization: it may be scheduled while
+// its predecessor drains, and waits for it (complete, writes visible) before touching memory.  A copy, a
+// kernel that is not a template's, or the segment's first entry keeps the full ordering.
+static int plan_issue(tc_plan* plan, size_t b, size_t end, CUstream st) {
   bool prev_kernel = false;
-  for (auto& e : plan->entries) {
+  for (size_t i = b; i < end; i++) {
+    auto& e = plan->entries[i];
     if (e.kind == 2) {
       if (e.bytes) CU_TRY(CU(cuMemcpyDtoDAsync)((CUdeviceptr)e.dst, (CUdeviceptr)e.src, e.bytes, st));
       prev_kernel = false;
@@ -745,17 +775,45 @@ static int plan_issue(tc_plan* plan) {
   return TC_OK;
 }
 
+// The segments of a plan: the runs of entries between its allreduce entries (possibly empty).
+static std::vector<std::pair<size_t, size_t>> plan_segments(const tc_plan* plan) {
+  std::vector<std::pair<size_t, size_t>> segs;
+  size_t b = 0;
+  for (size_t i = 0; i < plan->entries.size(); i++)
+    if (plan->entries[i].kind == 3) { segs.push_back({b, i}); b = i + 1; }
+  segs.push_back({b, plan->entries.size()});
+  return segs;
+}
+
+// Segment by segment on the plan's stream; after segment k, allreduce entry k is enqueued on the
+// collective stream behind an event of the plan's stream, so it runs while segment k+1 computes.  The
+// plan's stream waits for the collective stream at the end: the next work on it sees every sum.
+static int plan_run(tc_plan* plan) {
+  CUstream st = plan->ctx->stream;
+  auto segs = plan_segments(plan);
+  for (size_t k = 0; k < segs.size(); k++) {
+    if (plan->captured) {
+      if (plan->execs[k]) CU_TRY(CU(cuGraphLaunch)(plan->execs[k], st));
+    } else if (int s = plan_issue(plan, segs[k].first, segs[k].second, st)) {
+      return s;
+    }
+    if (k + 1 == segs.size()) break;
+    auto& c = plan->entries[segs[k].second];
+    CU_TRY(CU(cuEventRecord)(c.ready, st));
+    CU_TRY(CU(cuStreamWaitEvent)(plan->coll, c.ready, 0));
+    if (int s = tc_allreduce_f32_on(c.comm, c.dst, c.bytes, c.scale, (uint64_t)(uintptr_t)plan->coll)) return s;
+  }
+  if (segs.size() > 1) {
+    CU_TRY(CU(cuEventRecord)(plan->joined, plan->coll));
+    CU_TRY(CU(cuStreamWaitEvent)(st, plan->joined, 0));
+  }
+  return TC_OK;
+}
+
 int tc_plan_run(tc_plan* plan) {
   if (!plan) return fail(TC_ERR_INVALID, "null plan");
   if (int s = bind(plan->ctx)) return s;
-  if (plan->exec) {
-    if (plan->captured_on != plan->ctx->stream) {
-      // graphs replay on any stream of the context
-    }
-    CU_TRY(CU(cuGraphLaunch)(plan->exec, plan->ctx->stream));
-    return TC_OK;
-  }
-  return plan_issue(plan);
+  return plan_run(plan);  // a captured plan's graphs replay on any stream of the context
 }
 
 int tc_plan_run_on(tc_plan* plan, uint64_t stream) {
@@ -767,28 +825,45 @@ int tc_plan_run_on(tc_plan* plan, uint64_t stream) {
   return s;
 }
 
+static void plan_drop_graphs(tc_plan* plan) {
+  for (auto x : plan->execs) if (x) CU(cuGraphExecDestroy)(x);
+  for (auto g : plan->graphs) if (g) CU(cuGraphDestroy)(g);
+  plan->execs.clear();
+  plan->graphs.clear();
+}
+
 int tc_plan_capture(tc_plan* plan) {
   if (!plan) return fail(TC_ERR_INVALID, "null plan");
   if (int s = bind(plan->ctx)) return s;
-  if (plan->exec) return TC_OK;
+  if (plan->captured) return TC_OK;
   CUstream st = plan->ctx->stream;
-  CU_TRY(CU(cuStreamBeginCapture)(st, CU_STREAM_CAPTURE_MODE_THREAD_LOCAL));
-  int s = plan_issue(plan);
-  CUgraph g = nullptr;
-  CUresult r = CU(cuStreamEndCapture)(st, &g);
-  if (s) { if (g) CU(cuGraphDestroy)(g); return s; }
-  if (r != CUDA_SUCCESS) return fail(TC_ERR_CUDA, "cuStreamEndCapture: %s", cu_name(r));
-  r = CU(cuGraphInstantiate)(&plan->exec, g, 0);
-  if (r != CUDA_SUCCESS) { CU(cuGraphDestroy)(g); return fail(TC_ERR_CUDA, "cuGraphInstantiate: %s", cu_name(r)); }
-  plan->graph = g;
-  plan->captured_on = st;
+  for (auto& seg : plan_segments(plan)) {
+    CUgraph g = nullptr;
+    CUgraphExec x = nullptr;
+    if (seg.second > seg.first) {
+      CU_TRY(CU(cuStreamBeginCapture)(st, CU_STREAM_CAPTURE_MODE_THREAD_LOCAL));
+      int s = plan_issue(plan, seg.first, seg.second, st);
+      CUresult r = CU(cuStreamEndCapture)(st, &g);
+      if (s) { if (g) CU(cuGraphDestroy)(g); plan_drop_graphs(plan); return s; }
+      if (r != CUDA_SUCCESS) { plan_drop_graphs(plan); return fail(TC_ERR_CUDA, "cuStreamEndCapture: %s", cu_name(r)); }
+      r = CU(cuGraphInstantiate)(&x, g, 0);
+      if (r != CUDA_SUCCESS) {
+        CU(cuGraphDestroy)(g);
+        plan_drop_graphs(plan);
+        return fail(TC_ERR_CUDA, "cuGraphInstantiate: %s", cu_name(r));
+      }
+    }
+    plan->graphs.push_back(g);
+    plan->execs.push_back(x);
+  }
+  plan->captured = true;
   return TC_OK;
 }
 
 int tc_plan_launch_count(tc_plan* plan, int* n) {
   if (!plan || !n) return fail(TC_ERR_INVALID, "null argument");
   int k = 0;
-  for (auto& e : plan->entries) if (e.kind != 2) k++;
+  for (auto& e : plan->entries) if (e.kind < 2) k++;
   *n = k;
   return TC_OK;
 }
@@ -796,8 +871,10 @@ int tc_plan_launch_count(tc_plan* plan, int* n) {
 int tc_plan_free(tc_plan* plan) {
   if (!plan) return TC_OK;
   CU(cuCtxSetCurrent)(plan->ctx->cu);
-  if (plan->exec) CU(cuGraphExecDestroy)(plan->exec);
-  if (plan->graph) CU(cuGraphDestroy)(plan->graph);
+  plan_drop_graphs(plan);
+  for (auto& e : plan->entries) if (e.ready) CU(cuEventDestroy)(e.ready);
+  if (plan->joined) CU(cuEventDestroy)(plan->joined);
+  if (plan->coll) CU(cuStreamDestroy)(plan->coll);
   delete plan;
   return TC_OK;
 }

@@ -1,14 +1,17 @@
-"""Data-parallel training over the batch: one process per GPU, one NCCL allreduce per step.
+"""Data-parallel training over the batch: one process per GPU, the gradients sum-allreduced over NCCL.
 
 The step is split where the reference's step builder exposes the gradients
 (src/m3b/step.js:18-31): a gradient graph (forward + loss + autodiff
 backward) run on this rank's shard of the batch, then an Adam graph
 (src/m3b/adam.js:24-48) run identically on every rank, so parameters stay
-replicated.  Between them, every gradient -- laid out back to back in one flat
-device buffer that the gradient graph writes directly -- is sum-allreduced
-once over NVLink/NVSwitch and scaled by 1/W (each rank's loss divides by its
-local row count, src/m3b/model.js:127-130, so the average of the rank
-gradients is the full-batch gradient).  World size 1 skips the collective.
+replicated.  Every gradient -- laid out back to back in one flat device buffer
+that the gradient graph writes directly -- is sum-allreduced over
+NVLink/NVSwitch and scaled by 1/W (each rank's loss divides by its local row
+count, src/m3b/model.js:127-130, so the average of the rank gradients is the
+full-batch gradient).  The buffer is ordered by when the backward finishes each
+gradient and cut into a few contiguous buckets; each bucket's allreduce runs on
+a collective stream while the rest of the backward computes, and the Adam graph
+waits for all of them.  World size 1 skips the collective.
 
 Process plumbing (rank, world, the NCCL unique id) goes through
 torch.distributed's gloo group on the host; the collective itself is the
@@ -18,6 +21,7 @@ waits).  No TMA, no multicast: remote data arrives only through NCCL.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 
@@ -28,6 +32,24 @@ from . import runtime as rt
 from . import steps as _steps
 
 COMM_TIMEOUT_MS = 120000
+DEFAULT_BUCKETS = 4
+
+
+def bucket_layout(nbytes, buckets):
+    """Offsets of tensors of `nbytes` laid out back to back in this order (256-byte aligned slices), and
+    at most `buckets` contiguous spans (lo, hi, first index, end index) covering the whole layout, cut
+    at tensor boundaries into about equal bytes: a tensor that starts in a later `buckets`-th of the
+    total than the current span's first tensor opens a new span."""
+    offs, total = [], 0
+    for n in nbytes:
+        offs.append(total)
+        total += (n + 255) // 256 * 256
+    spans, start = [], 0
+    for j in range(1, len(offs) + 1):
+        if j == len(offs) or offs[j] * buckets // max(total, 1) > offs[start] * buckets // max(total, 1):
+            spans.append((offs[start], offs[j] if j < len(offs) else total, start, j))
+            start = j
+    return offs, spans
 
 
 class Comm:
@@ -67,10 +89,16 @@ class DPTrainer:
     """The transformer training step, data parallel.  `batch_local` sequences per rank."""
 
     def __init__(self, runner, V, batch_local, cfg, params, state=None, comm=None, opt=_steps.ADAM_3B,
-                 matmul="tiled", capture=True, batch=True, colfuse=True, mofuse=True):
+                 matmul="tiled", capture=True, batch=True, colfuse=True, mofuse=True, buckets=None):
         """`colfuse`: every bias gradient (a sum over axis 0) runs inside its elementwise producer's
         launch (codegen.colsum_fusions); `mofuse`: an elementwise reader runs in its producer's pass
-        (codegen.mo_fusions).  Values are bitwise those of the separate launches either way."""
+        (codegen.mo_fusions).  Values are bitwise those of the separate launches either way.
+
+        `buckets` (world > 1; default $TCB_DP_BUCKETS, else DEFAULT_BUCKETS): the flat gradient buffer
+        is laid out in the order the backward finishes the gradients and cut into that many contiguous
+        buckets of about equal bytes; each bucket's allreduce is issued on the collective stream as soon
+        as its last gradient is written, so it runs while the rest of the backward computes.  1 = one
+        allreduce of the whole buffer after the gradient program."""
         self.runner, self.comm = runner, comm
         gs = _steps.build_grad3b(V, batch_local, cfg)
         ad = _steps.build_adam_graph(V, cfg, opt)
@@ -82,24 +110,51 @@ class DPTrainer:
         fg = fuse(gs["graph"], keep=keep)
         self.loss_id = fg.index[gs["loss"]]
         grad_ids = [fg.index[gs["grads"][n]] for n in names]
-        # one flat gradient buffer, each gradient at its offset (256-byte aligned slices)
-        offs, total = [], 0
-        for n in names:
-            offs.append(total)
-            total += (size(shapes[n]) * 4 + 255) // 256 * 256
-        self.flat = rt.DeviceBuffer(runner, total)
-        self.flat_floats = total // 4
-        rt.check(rt.lib().tc_memset32(runner.ctx, self.flat.ptr, 0, self.flat_floats))  # padding, zero gradients
-        # parameters: one buffer each, shared by both graphs (the Adam graph's outputs are copied back)
-        self.params = {n: rt.DeviceBuffer(runner, size(shapes[n]) * 4) for n in names}
-        place_g = {fg.index[gs["inputs"][n]]: self.params[n].ptr for n in names}
-        # a gradient the graph gives as a constant zero (no dependence) is still written by its launch
-        for gid, off in zip(grad_ids, offs):
-            place_g[gid] = self.flat.ptr + off
         lowered_g = lower_fused(fg.graph, matmul=matmul, fold=True, keep=[self.loss_id, *grad_ids], colfuse=colfuse,
                                 mofuse=mofuse)
         self.lowered_g = lowered_g
-        self.grad_prog = rt.Program(runner, fg.graph, lowered_g, keep=[self.loss_id], place=place_g, batch=batch)
+        w = comm.world if comm is not None else 1
+        if buckets is None:
+            buckets = int(os.environ.get("TCB_DP_BUCKETS", DEFAULT_BUCKETS))
+        self.buckets = max(1, buckets) if w > 1 else 1
+        input_ids = [fg.index[gs["inputs"][n]] for n in names]
+        order = list(range(len(names)))
+        if self.buckets > 1:
+            launches, _, _ = rt.select_launches(fg.graph, lowered_g, keep=[self.loss_id],
+                                                place=set(input_ids) | set(grad_ids), batch=batch)
+            done = {}
+            for k, lau in enumerate(launches):
+                for nid in getattr(lau, "nodes", [lau.node]):
+                    done[nid] = k
+            order.sort(key=lambda j: (done.get(grad_ids[j], -1), j))
+        # one flat gradient buffer, each gradient at its offset (256-byte aligned slices)
+        offs, spans = bucket_layout([size(shapes[names[j]]) * 4 for j in order], self.buckets)
+        self.order = [names[j] for j in order]
+        at = dict(zip(order, offs))
+        offs = [at[j] for j in range(len(names))]
+        total = spans[-1][1] if spans else 0
+        self.flat = rt.DeviceBuffer(runner, max(total, 256))
+        self.flat_floats = total // 4
+        rt.check(rt.lib().tc_memset32(runner.ctx, self.flat.ptr, 0, max(total, 256) // 4))  # padding, zero grads
+        # parameters: one buffer each, shared by both graphs (the Adam graph's outputs are copied back)
+        self.params = {n: rt.DeviceBuffer(runner, size(shapes[n]) * 4) for n in names}
+        place_g = {iid: self.params[n].ptr for iid, n in zip(input_ids, names)}
+        # a gradient the graph gives as a constant zero (no dependence) is still written by its launch
+        for gid, off in zip(grad_ids, offs):
+            place_g[gid] = self.flat.ptr + off
+        # With a power-of-two world the 1/W of the mean goes into the cotangent seed: backpropagation is
+        # linear in it and a power-of-two scale is exact in every operation, so each rank's gradients
+        # come out as exactly 1/W times its own, and the allreduce is a plain sum.
+        self.prescaled = w > 1 and (w & (w - 1)) == 0
+        colls = []
+        self.bucket_spans = [(lo, hi) for lo, hi, _, _ in spans]
+        if self.buckets > 1:
+            scale = 1.0 if self.prescaled else 1.0 / w
+            for lo, hi, a, b in spans:
+                colls.append(([grad_ids[order[i]] for i in range(a, b)], self.flat.ptr + lo, (hi - lo) // 4, scale,
+                              comm.handle))
+        self.grad_prog = rt.Program(runner, fg.graph, lowered_g, keep=[self.loss_id], place=place_g, batch=batch,
+                                    collectives=colls)
         fa = fuse(ad["graph"], keep=list(ad["outputs"].values()))
         place_a = {}
         for n, off in zip(names, offs):
@@ -118,12 +173,7 @@ class DPTrainer:
             state = _steps.adam_initial_state(names, shapes)
         for k in state_names:
             self.adam_prog.write(fa.index[ad["inputs"][k]], state[k])
-        # With a power-of-two world the 1/W of the mean goes into the cotangent seed: backpropagation is
-        # linear in it and a power-of-two scale is exact in every operation, so each rank's gradients
-        # come out as exactly 1/W times its own, and the allreduce is a plain sum.
         cot = fg.graph.input_id(gs["cotangent"])
-        w = comm.world if comm is not None else 1
-        self.prescaled = w > 1 and (w & (w - 1)) == 0
         self.grad_prog.write(cot, [1.0 / w if self.prescaled else 1.0])
         self.x_id = fg.index[gs["inputs"]["x"]]
         self.y_id = fg.index[gs["inputs"]["y"]]
@@ -134,8 +184,8 @@ class DPTrainer:
 
     def step_device(self):
         """One step with x, y already on the device: gradients, allreduce, Adam (asynchronous)."""
-        self.grad_prog.run()
-        if self.comm is not None and self.comm.world > 1:
+        self.grad_prog.run()   # with buckets, the allreduces run inside it
+        if self.comm is not None and self.comm.world > 1 and self.buckets == 1:
             self.comm.allreduce_mean(self.flat.ptr, self.flat_floats, prescaled=self.prescaled)
         self.adam_prog.run()
 

@@ -103,6 +103,8 @@ _SIGS = {
                                 ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint32, ctypes.c_int,
                                 ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(Args)], ctypes.c_int),
     "tc_plan_add_copy": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "tc_plan_add_allreduce": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float],
+                              ctypes.c_int),
     "tc_plan_run": ([ctypes.c_void_p], ctypes.c_int),
     "tc_plan_capture": ([ctypes.c_void_p], ctypes.c_int),
     "tc_plan_launch_count": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
@@ -132,6 +134,8 @@ _SIGS = {
     "tc_comm_init": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
                       ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "tc_allreduce_f32": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float], ctypes.c_int),
+    "tc_allreduce_f32_on": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, ctypes.c_uint64],
+                            ctypes.c_int),
     "tc_comm_wait": ([ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
     "tc_comm_abort": ([ctypes.c_void_p], ctypes.c_int),
     "tc_comm_destroy": ([ctypes.c_void_p], ctypes.c_int),
@@ -569,6 +573,44 @@ def batch_small_launches(launches, root, max_elems=BATCH_MAX_ELEMS):
     return out
 
 
+def select_launches(graph, lowered, keep=(), feedback=(), place=(), alias=True, batch=False, prune=True):
+    """The launches a resident program over `lowered` issues, in order (Program's `prune`, `alias` and
+    `batch` rules), with the alias map (reshape node -> its source) and the number pruned.  A pure
+    function of its arguments: a caller that lays out memory by launch order (the data-parallel
+    trainer's bucketed gradient buffer) gets the order the program will have."""
+    nodes = graph.nodes
+    keep = set(keep)
+    place = set(place)
+    fb = {i for pair in feedback for i in pair}
+    amap = {}
+    out = []
+    live = None
+    if prune:
+        live = set(keep) | {src for src, _ in feedback} | place
+        for n in reversed(nodes):
+            if n.id in live:
+                live.update(n.inputs)
+    pruned = 0
+    for lau in lowered["launches"]:
+        if live is not None and not any(n in live for n in getattr(lau, "nodes", [lau.node])):
+            pruned += 1
+            continue
+        n = nodes[lau.node]
+        if (alias and n.op == "reshape" and lau.kind == "gather" and lau.node not in keep
+                and lau.node not in place and lau.node not in fb):
+            amap[lau.node] = lau.inputs[0]
+            continue
+        out.append(lau)
+
+    def root(i):
+        while i in amap:
+            i = amap[i]
+        return i
+    if batch:
+        out = batch_small_launches(out, root)
+    return out, amap, pruned
+
+
 class Program:
     """A lowered graph made resident on the device, replayed by a native plan.
 
@@ -581,8 +623,13 @@ class Program:
     """
 
     def __init__(self, runner, graph, lowered, keep=(), feedback=(), capture=False, place=None, alias=True,
-                 batch=False, prune=True):
+                 batch=False, prune=True, collectives=()):
         """`place` maps node ids to device addresses owned by the caller (e.g. slices of one flat buffer).
+
+        `collectives`: (node ids, device address, float count, scale, communicator handle) tuples -- a
+        sum-allreduce of that range, issued on the plan's collective stream right after the last launch
+        that writes any of those nodes, so the launches after it compute while it runs
+        (tc_plan_add_allreduce); the plan's end waits for all of them.
 
         `prune`: launches whose values nothing reads -- no kept, fed-back or caller-placed value depends
         on them (autodiff's branches toward constants, say) -- are left out; every value the program
@@ -600,32 +647,12 @@ class Program:
         keep = set(keep)
         place = place or {}
         fb = {i for pair in feedback for i in pair}
-        self.alias = {}
-        launches = []
-        live = None
-        if prune:
-            live = set(keep) | {src for src, _ in feedback} | set(place)
-            for n in reversed(nodes):
-                if n.id in live:
-                    live.update(n.inputs)
-        self.pruned = 0
-        for lau in lowered["launches"]:
-            if live is not None and not any(n in live for n in getattr(lau, "nodes", [lau.node])):
-                self.pruned += 1
-                continue
-            n = nodes[lau.node]
-            if (alias and n.op == "reshape" and lau.kind == "gather" and lau.node not in keep
-                    and lau.node not in place and lau.node not in fb):
-                self.alias[lau.node] = lau.inputs[0]
-                continue
-            launches.append(lau)
+        launches, self.alias, self.pruned = select_launches(graph, lowered, keep, feedback, place, alias, batch, prune)
 
         def root(i):
             while i in self.alias:
                 i = self.alias[i]
             return i
-        if batch:
-            launches = batch_small_launches(launches, root)
         self.launches = launches
         first, last = {}, {}
         for k, lau in enumerate(self.launches):
@@ -691,12 +718,22 @@ class Program:
         self._hoist = None
         if batch:
             self.kernel_launches += self._hoist_input_splits(h)
+        done_at = {}
+        for k, lau in enumerate(self.launches):
+            for nid in getattr(lau, "nodes", [lau.node]):
+                done_at[nid] = k
+        after = {}
+        for ids, ptr, count, scale, comm in collectives:
+            after.setdefault(max(done_at[i] for i in ids), []).append((ptr, count, scale, comm))
+        self.collectives = len(collectives)
         for k, lau in enumerate(self.launches):
             for call in program_calls(lau):
                 if k in self.hoisted and call.name == "tcb_split_b":
                     continue
                 self.issue_call(k, lau, call, h)
                 self.kernel_launches += 1
+            for ptr, count, scale, comm in after.get(k, ()):
+                check(lib().tc_plan_add_allreduce(h, comm, ptr, count, ctypes.c_float(scale)))
         if batch and feedback:
             self.kernel_launches += self._issue_copies(feedback, h)
         else:

@@ -21,9 +21,12 @@ def _gpus():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-def test_two_ranks_match_one_gpu(tmp_path):
+@pytest.mark.parametrize("buckets", ["4", "1"])
+def test_two_ranks_match_one_gpu(tmp_path, buckets):
+    """`buckets` 4: the gradient buckets are reduced on the collective stream during the backward; 1: one
+    allreduce after it."""
     worker = os.path.join(ROOT, "tests", "dp_worker.py")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TCB_DP_BUCKETS=buckets)
     one, two = tmp_path / "one.npz", tmp_path / "two.npz"
     subprocess.run([sys.executable, worker, str(one), "2", "8"], check=True, timeout=600, env=env)
     subprocess.run(["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",

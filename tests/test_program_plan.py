@@ -89,6 +89,10 @@ class Recorder:
         self.plans[plan.value].append(("copy", int(dst), int(src), int(nbytes)))
         return 0
 
+    def tc_plan_add_allreduce(self, plan, comm, buf, count, scale):
+        self.plans[plan.value].append(("allreduce", int(buf), int(count), float(scale.value), comm))
+        return 0
+
     def tc_plan_capture(self, plan):
         return 0
 
@@ -157,13 +161,18 @@ def _replay(prog, graph):
             write(o)
 
 
-def _dp_trainer(pkg, runner, batch, full=False):
+def _dp_trainer(pkg, runner, batch, full=False, comm=None, buckets=None):
     wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
     dp = importlib.import_module("tensor-compiler-webgpu_b200.dp")
     cfg, c = wl.c5_cfg(batch=512) if full else wl.c5_cfg(d=64, L=2, H=4, ff=128, T=32, batch=4)
     V, B = c["V"], c["batch"]
     params = pkg.steps.init_params_normal(V, 0, 0.02, cfg)
-    return dp.DPTrainer(runner, V, B, cfg, params, batch=batch, capture=False)
+    return dp.DPTrainer(runner, V, B, cfg, params, batch=batch, capture=False, comm=comm, buckets=buckets)
+
+
+class _FakeComm:
+    def __init__(self, world):
+        self.world, self.handle = world, ctypes.c_void_p(0x5eed)
 
 
 @pytest.mark.parametrize("batch,full", [(False, False), (True, False), (True, True)])
@@ -240,3 +249,48 @@ def test_replay_catches_a_clobbered_value(pkg, recorded, monkeypatch):
     tr = _dp_trainer(pkg, runner, True)
     with pytest.raises(AssertionError, match="memory was reused|overlap"):
         _replay(tr.grad_prog, tr.fg.graph)
+
+
+@pytest.mark.parametrize("world,buckets,full", [(4, 4, False), (8, 4, True), (3, 2, False), (2, 1, False)])
+def test_bucketed_allreduce_plan(pkg, recorded, world, buckets, full):
+    """Data parallel with the gradient buckets reduced during the backward: the buckets tile the flat
+    gradient buffer exactly, each allreduce is planned after every launch that writes a gradient of its
+    bucket, and no launch after it reads or writes its range (it runs on another stream meanwhile).
+    Power-of-two worlds reduce a plain sum (the 1/W is in the cotangent seed), others scale by 1/W."""
+    rt, rec, runner = recorded
+    tr = _dp_trainer(pkg, runner, True, full, comm=_FakeComm(world), buckets=buckets)
+    gp = tr.grad_prog
+    entries = rec.plans[gp.plan.value]
+    colls = [(k, e) for k, e in enumerate(entries) if e[0] == "allreduce"]
+    if buckets == 1:
+        assert not colls and tr.buckets == 1
+        return
+    assert 2 <= len(colls) <= buckets
+    base = tr.flat.ptr
+    spans = sorted((e[1] - base, e[1] - base + 4 * e[2]) for _, e in colls)
+    assert spans[0][0] == 0 and spans[-1][1] == 4 * tr.flat_floats
+    assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    want_scale = float(np.float32(1.0 if world & (world - 1) == 0 else 1.0 / world))
+    assert all(e[3] == want_scale for _, e in colls)
+    grads = [tr.fg.index[tr.gs["grads"][n]] for n in tr.names]
+    nbytes = {g: 4 * int(np.prod(tr.fg.graph.nodes[g].shape, dtype=np.int64)) for g in grads}
+    launch_entries = [k for k, e in enumerate(entries) if e[0] == "launch"]
+    assert len(launch_entries) == gp.kernel_launches
+
+    def touches(e, lo, hi):
+        a = e[3]
+        ptrs = [a["out"], *[p for p in a["in"] if p]]
+        if e[1] == "tcb_elementwise_mo":
+            ptrs += [p for p in a["p"][1:4] if p]
+        return any(lo <= p < hi for p in ptrs)
+    for k, e in colls:
+        lo, hi = e[1], e[1] + 4 * e[2]
+        members = [g for g in grads if lo <= gp.ptrs[g] < hi]
+        assert members and all(gp.ptrs[g] + nbytes[g] <= hi for g in members)
+        assert any(touches(entries[j], lo, hi) for j in launch_entries if j < k)
+        for j in launch_entries:
+            if j > k:
+                assert not touches(entries[j], lo, hi), (k, j, entries[j][1])
+    # the layout follows the order in which the backward finishes the gradients
+    at = [gp.ptrs[tr.fg.index[tr.gs["grads"][n]]] for n in tr.order]
+    assert at == sorted(at)
