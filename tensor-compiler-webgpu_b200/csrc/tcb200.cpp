@@ -645,8 +645,11 @@ struct tc_plan {
     CUevent ready = nullptr;  // an allreduce: recorded on the plan's stream, waited for by the collective stream
   };
   std::vector<Entry> entries;
-  // Programmatic dependent launch between consecutive template kernels ($TCB_PDL=0 turns it off).
-  bool pdl = true;
+  // Programmatic dependent launch between consecutive template kernels: $TCB_PDL=0 never, 1 always, unset
+  // (the default) only where both grids fit in one wave (at most one CTA per SM).  Measured on the B200: a
+  // chain of one-wave kernels (the C1 step) gains 9 %; the transformer step, whose kernels fill the GPU,
+  // loses 6 % with every edge programmatic.
+  int pdl = 2;
   // Captured form: one graph per segment between allreduce entries (a collective is never captured; it is
   // enqueued between the segments' graph launches).  Empty segments have none.
   bool captured = false;
@@ -665,7 +668,7 @@ int tc_plan_create(tc_ctx* ctx, tc_plan** out) {
   *out = new tc_plan();
   (*out)->ctx = ctx;
   const char* e = getenv("TCB_PDL");
-  (*out)->pdl = !(e && e[0] == '0');
+  (*out)->pdl = e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : 2;
   return TC_OK;
 }
 
@@ -736,11 +739,14 @@ int tc_plan_add_allreduce(tc_plan* plan, tc_comm* comm, uint64_t buf, uint64_t c
 }
 
 // Entries [b, end) of one segment (kernels and copies) on `st`.  A template kernel that follows another
-// kernel of the segment is launched with programmatic stream serialization: it may be scheduled while
-// its predecessor drains, and waits for it (complete, writes visible) before touching memory.  A copy, a
-// kernel that is not a template's, or the segment's first entry keeps the full ordering.
+// kernel of the segment is launched with programmatic stream serialization (where the plan's policy
+// allows it for the two grids): it may be scheduled while its predecessor drains, and waits for it
+// (complete, writes visible) before touching memory.  A copy, a kernel that is not a template's, or the
+// segment's first entry keeps the full ordering.
 static int plan_issue(tc_plan* plan, size_t b, size_t end, CUstream st) {
   bool prev_kernel = false;
+  uint64_t prev_ctas = 0;
+  const uint64_t wave = (uint64_t)plan->ctx->sm_count;
   for (size_t i = b; i < end; i++) {
     auto& e = plan->entries[i];
     if (e.kind == 2) {
@@ -748,11 +754,14 @@ static int plan_issue(tc_plan* plan, size_t b, size_t end, CUstream st) {
       prev_kernel = false;
       continue;
     }
+    const uint64_t ctas = (uint64_t)e.grid[0] * e.grid[1] * e.grid[2];
+    const bool pdl = plan->pdl == 1 || (plan->pdl == 2 && ctas <= wave && prev_ctas <= wave);
+    prev_ctas = ctas;
     void* params[1];
     tc_args a = e.args;
     if (e.kind == 1) params[0] = e.tma.get();
     else params[0] = &a;
-    if (plan->pdl && e.waits && prev_kernel) {
+    if (pdl && e.waits && prev_kernel) {
       CUlaunchAttribute attr[1];
       memset(attr, 0, sizeof attr);
       attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
