@@ -794,12 +794,14 @@ def fused_split_plan(batch, M, K, N, bn, a_t=False, b_t=False):
 
 
 def gemm_bn(N):
-    """Accumulator width: 256 TMEM columns when N fills them, else 128 (TCB_GEMM_BN overrides)."""
+    """Accumulator width: 256 TMEM columns when N fills them, 64 when N <= 64 (the batched attention
+    products with a head dimension of 64: a wider tile would spend half its tensor-core work on
+    padding), else 128 (TCB_GEMM_BN overrides)."""
     import os
     forced = os.environ.get("TCB_GEMM_BN")
     if forced:
         return int(forced)
-    return 256 if N >= 256 else 128
+    return 256 if N >= 256 else 64 if N <= 64 else 128
 
 
 def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage=None, a_t=False, b_t=False):
@@ -1096,19 +1098,24 @@ def _matmul_operands(graph, node):
 
 
 def foldable_transposes(graph, matmul, keep=()):
-    """Plain transposeLast2 nodes read only as tensor-core GEMM operands: their launch can be dropped and the
-    GEMM's operand split reads the transpose's source instead (the split rewrites the layout anyway)."""
+    """Plain transposeLast2 nodes read only as tensor-core GEMM operands, or by other such nodes that fold:
+    their launch can be dropped and the GEMM's operand split reads the source at the end of the chain
+    instead (the split rewrites the layout anyway; two swaps cancel).  Autodiff makes such chains: the
+    backward of x^T reads transpose(x^T).  Readers come after what they read, so one pass from the end
+    sees every reader's verdict first."""
     keep = set(keep)
     consumers = {}
     for n in graph.nodes:
         for i in n.inputs:
             consumers.setdefault(i, []).append(n)
     folds = set()
-    for t in graph.nodes:
+    for t in reversed(graph.nodes):
         if t.op != "transpose" or t.id in keep or not _is_last2_swap(t) or t.id not in consumers:
             continue
         ok = True
         for c in consumers[t.id]:
+            if c.id in folds:
+                continue
             ops = _matmul_operands(graph, c)
             if ops is None or t.id not in ops or not uses_tensor_cores(graph.nodes[ops[0]].shape, matmul):
                 ok = False
@@ -1118,11 +1125,19 @@ def foldable_transposes(graph, matmul, keep=()):
     return folds
 
 
+def _unfold(graph, i, folds):
+    """(the node a GEMM operand slot reads through a chain of folded transposes, whether it is transposed)."""
+    t = False
+    while i in folds:
+        i, t = graph.nodes[i].inputs[0], not t
+    return i, t
+
+
 def _folded_launch(graph, node, matmul, sabotage, folds):
     """The GEMM launch of `node` with folded transposed operands substituted by their sources."""
     from .fuse import body_of
     a, b = _matmul_operands(graph, node)
-    a_t, b_t = a in folds, b in folds
+    a_t, b_t = _unfold(graph, a, folds)[1], _unfold(graph, b, folds)[1]
     if node.op == "matmul":
         shapes = [list(graph.nodes[i].shape) for i in node.inputs]
         body, out = _one_op_body("matmul", shapes, node.attrs)
@@ -1132,7 +1147,7 @@ def _folded_launch(graph, node, matmul, sabotage, folds):
         lau = _epilogue_launch(body_of(node), node.attrs["output"], node.id, "fused", "fused-epilogue",
                                node.attrs["pattern"], list(node.inputs), matmul,
                                sabotage if sabotage in FUSED_SABOTAGE else None, a_t, b_t)
-    lau.inputs = [graph.nodes[i].inputs[0] if i in folds else i for i in node.inputs]
+    lau.inputs = [_unfold(graph, i, folds)[0] for i in node.inputs]
     return lau
 
 

@@ -893,7 +893,7 @@ static i64 gemm_stages(i64 bn, i64 bk) {
 static i64 gemm_smem(i64 bn, i64 bk) { return gemm_stages(bn, bk) * gemm_stage_bytes(bn, bk) + 1024 + GEMM_STAGING + 1024; }
 static bool tma_store_ok(i64 N) { return N % 4 == 0; }
 static i64 gemm_bk(i64 bn) { return bn == 256 ? 16 : 32; }
-static i64 gemm_bn(i64 N) { return N >= 256 ? 256 : 128; }
+static i64 gemm_bn(i64 N) { return N >= 256 ? 256 : N <= 64 ? 64 : 128; }
 static i64 split_bytes(i64 batch, i64 M, i64 K, i64 N, std::pair<bool, bool> fs) {
   i64 Kp = kpad(K);
   return (fs.first ? 0 : 2 * batch * M * Kp * 4) + (fs.second ? 0 : 2 * batch * N * Kp * 4);
@@ -1235,10 +1235,14 @@ static std::set<int> foldable_transposes(const Graph& g, const std::string& matm
   for (auto& n : g.nodes)
     for (int i : n.inputs) consumers[i].push_back(n.id);
   std::set<int> folds;
-  for (auto& t : g.nodes) {
+  // readers come after what they read: from the end, every reader's verdict is known (a reader that is a
+  // folded transposeLast2 is fine: the GEMMs behind it read through the chain)
+  for (auto it = g.nodes.rbegin(); it != g.nodes.rend(); ++it) {
+    const Node& t = *it;
     if (t.op != "transpose" || keep.count(t.id) || !is_last2_swap(t) || !consumers.count(t.id)) continue;
     bool ok = true;
     for (int c : consumers[t.id]) {
+      if (folds.count(c)) continue;
       std::pair<int, int> ab;
       if (!matmul_operands(g, g.nodes[c], &ab) || (ab.first != t.id && ab.second != t.id) ||
           !uses_tensor_cores(g.nodes[ab.first].shape, matmul)) {
@@ -1263,7 +1267,15 @@ static Launch folded_launch(Lowering& L, const Node& node, const std::string& ma
   const Graph& g = *L.graph;
   std::pair<int, int> ab;
   matmul_operands(g, node, &ab);
-  bool a_t = folds.count(ab.first) > 0, b_t = folds.count(ab.second) > 0;
+  // a slot read through a chain of folded transposes: its source, transposed when the chain is odd
+  auto unfold = [&](int i, bool* t) {
+    *t = false;
+    while (folds.count(i)) { i = g.nodes[i].inputs[0]; *t = !*t; }
+    return i;
+  };
+  bool a_t = false, b_t = false;
+  unfold(ab.first, &a_t);
+  unfold(ab.second, &b_t);
   Launch l;
   if (node.op == "matmul") {
     std::vector<std::vector<i64>> shapes;
@@ -1276,7 +1288,8 @@ static Launch folded_launch(Lowering& L, const Node& node, const std::string& ma
                         sab_or_empty(sabotage), a_t, b_t);
   }
   l.inputs.clear();
-  for (int i : node.inputs) l.inputs.push_back(folds.count(i) ? g.nodes[i].inputs[0] : i);
+  bool t;
+  for (int i : node.inputs) l.inputs.push_back(unfold(i, &t));
   return l;
 }
 

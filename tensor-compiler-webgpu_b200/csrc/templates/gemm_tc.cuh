@@ -587,31 +587,22 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
         continue;
       }
       if (TCB_TMA_STORE) {
-        // 32 columns at a time: the fused body on this row's 32 values (split-K: the raw partial sums),
-        // written into a 128-byte-swizzled 32 x 32 staging block (conflict-free: 16-byte chunk c of row
-        // r at r * 128 + (c ^ (r & 7)) * 16), then one TMA store of the block -- to the output, or with
+        // 32 columns at a time: this row's 32 accumulator values (split-K: the raw partial sums) written
+        // into a 128-byte-swizzled 32 x 32 staging block (conflict-free: 16-byte chunk c of row r at
+        // r * 128 + (c ^ (r & 7)) * 16), then one TMA store of the block -- to the output, or with
         // split-K to this split's slice of the partial sums [SPLITK * batch, M, N]; two blocks per warp
-        // alternate.
-        const int r = 32 * q + lane;
+        // alternate.  The fused body runs on the staged block row by row, lane l on column c0 + l, so
+        // the operands it loads (a residual, another [M, N] value) are read 32 consecutive floats per
+        // warp instruction -- one 128-byte line -- where a thread per row would touch 32 lines.  Each
+        // element goes through the same operations as before: the values are unchanged.
         const int zc = TCB_SPLITK > 1 ? (int)(((t / S::TILES_PER) % TCB_SPLITK) * TCB_BATCH) + T.bz : T.bz;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32, ++nstore) {
           float v[32];
           tmem_ld16(tmem + buf * BN + ((u32)(32 * q) << 16) + (u32)c0, *reinterpret_cast<float(*)[16]>(&v[0]));
           tmem_ld16(tmem + buf * BN + ((u32)(32 * q) << 16) + (u32)(c0 + 16), *reinterpret_cast<float(*)[16]>(&v[16]));
-          const u64 grow = (u64)T.m0 + r;
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const u64 col = (u64)(T.n0 + c0 + jj);
-            const float acc = T.kb == 0 ? 0.0f : v[jj];
-            if (TCB_SPLITK > 1) {
-              v[jj] = acc;
-            } else {
-              v[jj] = (grow < (u64)TCB_M && col < (u64)TCB_N)
-                          ? Epi::apply(P.a, acc, (u64)T.bz * TCB_M * TCB_N + grow * TCB_N + col, grow, col, (u64)T.bz)
-                          : 0.0f;
-            }
-          }
+          for (int jj = 0; jj < 32; ++jj) v[jj] = T.kb == 0 ? 0.0f : v[jj];
           const u32 blk = staging + (u32)((q * 2 + (nstore & 1)) * 4096);
           if (lane == 0 && nstore >= 2) bulk_wait_read1();
           __syncwarp();
@@ -619,6 +610,25 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
 #pragma unroll
           for (int c = 0; c < 8; ++c)
             sp[lane * 8 + (c ^ (lane & 7))] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+          if (TCB_SPLITK == 1) {
+            // all 32 rows into registers before any result is written back: no store stands between the
+            // operand loads, so they are all in flight at once
+            __syncwarp();
+            float* sf = reinterpret_cast<float*>(sp);
+            const u64 col = (u64)(T.n0 + c0 + lane);
+            float o[32];
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) {
+              const u64 grow = (u64)T.m0 + 32 * q + rr;
+              const float acc = sf[rr * 32 + (((lane >> 2) ^ (rr & 7)) << 2) + (lane & 3)];
+              o[rr] = (grow < (u64)TCB_M && col < (u64)TCB_N)
+                          ? Epi::apply(P.a, acc, (u64)T.bz * TCB_M * TCB_N + grow * TCB_N + col, grow, col, (u64)T.bz)
+                          : 0.0f;
+            }
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) sf[rr * 32 + (((lane >> 2) ^ (rr & 7)) << 2) + (lane & 3)] = o[rr];
+            __syncwarp();
+          }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) {
