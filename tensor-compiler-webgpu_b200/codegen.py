@@ -726,7 +726,7 @@ def splitk_plan(batch, M, K, N, bn, fs=(False, False)):
     # up to 8 K ranges per tile are reduced inside the GEMM by the last arriver (tail_plan); split-K
     # with a finishing pass only when the SMs need more than that (tiles <= SMs / 9)
     if tiles < SM_COUNT and SM_COUNT // tiles > 8 and kb >= 8:
-        s = max(1, min(SM_COUNT // tiles, kb // 4, 64))
+        s = max(1, min(SM_COUNT // tiles, kb // 4))   # every SM: 2 tiles x 74 ranges, not 2 x 64
         s = math.ceil(kb / math.ceil(kb / s))  # no empty split
     part_off = split_bytes(batch, M, K, N, fs) + 256
     return s, part_off
@@ -1199,6 +1199,64 @@ def colsum_fusions(graph, keep=()):
     return out
 
 
+ROWSUM_MIN_ROWS = SM_COUNT * 8   # a warp per row: fewer rows would leave the producer's pass short of warps
+
+
+def rowsum_fusions(graph, keep=(), exclude=()):
+    """Sums over the last axis to fuse with their producer: {sum id: (producer id, write)}.
+
+    A `sum` over the last axis of an elementwise value (a fused elementwise node or a plain elementwise
+    op) with at least ROWSUM_MIN_ROWS rows is computed in the producer's pass (tcb/rowsum.cuh); `write`
+    as for column sums.  Sums and producers in `exclude` (already fused otherwise) are left alone."""
+    keep, exclude = set(keep), set(exclude)
+    consumers = {}
+    for n in graph.nodes:
+        for i in n.inputs:
+            consumers.setdefault(i, []).append(n.id)
+    out, taken = {}, set()
+    for S in graph.nodes:
+        if S.op != "sum" or S.id in exclude:
+            continue
+        P = graph.nodes[S.inputs[0]]
+        if (len(P.shape) < 2 or S.attrs["axis"] != len(P.shape) - 1 or P.id in taken or P.id in exclude
+                or size(P.shape[:-1]) < ROWSUM_MIN_ROWS or not _elementwise_producer(P)):
+            continue
+        out[S.id] = (P.id, P.id in keep or len(consumers[P.id]) > 1)
+        taken.add(P.id)
+    return out
+
+
+def _rowsum_launch(graph, P, S, write):
+    """One launch computing elementwise node P over [R, C] and S = its sum over the last axis
+    (tcb/rowsum.cuh), in tcb_reduce_rows's order, so the sums are bitwise the unfused pair's."""
+    from .fuse import body_of
+    if P.op == "fused":
+        body, out_id = body_of(P), P.attrs["output"]
+    else:
+        body, out_id = _one_op_body(P.op, [graph.nodes[i].shape for i in P.inputs], P.attrs)
+    R, C = size(P.shape[:-1]), P.shape[-1]
+    src = f"""// elementwise ({P.op}) + sum over the last axis of [{R}, {C}], value {'stored' if write else 'not stored'}
+#include "tcb/common.cuh"
+#define TCB_OUTER {R}
+#define TCB_N {C}
+#define TCB_INNER 1
+#define TCB_SPLIT 1
+#define TCB_IS_MAX 0
+#define TCB_WRITE {int(write)}
+{_ew_body_struct(body, out_id, R * C)}#include "tcb/rowsum.cuh"
+"""
+    main = KernelCall("tcb_ew_rowsum", (max(1, min(math.ceil(R * 32 / 256), SM_COUNT * 8)), 1, 1), (256, 1, 1))
+    if write:
+        main.ptr_params = ((14, S.id),)
+    lau = Launch(P.id if write else S.id, "fused", "fused-rowsum", "elementwise+rowsum", list(P.inputs), src, [main],
+                 info={"R": R, "C": C, "write": write, "producer": P.id, "sum": S.id})
+    if write:
+        lau.nodes = [P.id, S.id]
+    nbytes = sum(size(graph.nodes[i].shape) * 4 for i in dict.fromkeys(P.inputs)) + R * 4
+    lau.bytes = nbytes + (R * C * 4 if write else 0)
+    return lau
+
+
 def _colsum_launch(graph, P, S, write):
     """One launch computing elementwise node P over [R, C] and S = sum over axis 0 of it (tcb/colsum.cuh),
     with the plain column sum's split, so the sum is bitwise the unfused pair's."""
@@ -1404,15 +1462,19 @@ def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfu
     launch; the GEMM's operand split reads their source.  Their values then never exist on the device,
     so verification runs that read back every node lower without it.
     `colfuse` (resident programs only): a sum over axis 0 runs in its elementwise producer's launch
-    (colsum_fusions); a producer read by nothing else is then never stored.  `keep` names the values
-    that must exist after the launches.
+    (colsum_fusions), and so does a sum over the last axis of enough rows (rowsum_fusions); a producer
+    read by nothing else is then never stored.  `keep` names the values that must exist after the
+    launches.
     `mofuse` (resident programs only): an elementwise reader whose other operands already exist is
     computed in its elementwise producer's launch, both stored (mo_fusions).
     """
     folds = foldable_transposes(graph, matmul, keep) if fold else set()
     cols = colsum_fusions(graph, keep) if colfuse else {}
-    producer_of = {p: (sid, w) for sid, (p, w) in cols.items()}
-    mos = mo_fusions(graph, keep, exclude=set(cols) | set(producer_of) | folds) if mofuse else {}
+    rows = rowsum_fusions(graph, keep, exclude=set(cols) | {p for p, _ in cols.values()}) if colfuse else {}
+    sums = {**{sid: (p, w, _colsum_launch) for sid, (p, w) in cols.items()},
+            **{sid: (p, w, _rowsum_launch) for sid, (p, w) in rows.items()}}
+    producer_of = {p: (sid, w, f) for sid, (p, w, f) in sums.items()}
+    mos = mo_fusions(graph, keep, exclude=set(sums) | set(producer_of) | folds) if mofuse else {}
     readers = set(mos.values())
     launches = []
     for node in graph.nodes:
@@ -1421,15 +1483,15 @@ def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfu
         if node.id in mos:                # a producer computing its reader too
             launches.append(_mo_launch(graph, node, graph.nodes[mos[node.id]]))
             continue
-        if node.id in producer_of:        # the producer of a fused column sum
-            sid, write = producer_of[node.id]
+        if node.id in producer_of:        # the producer of a fused column or row sum
+            sid, write, make = producer_of[node.id]
             if write:
-                launches.append(_colsum_launch(graph, node, graph.nodes[sid], True))
+                launches.append(make(graph, node, graph.nodes[sid], True))
             continue
-        if node.id in cols:               # the column sum itself
-            pid, write = cols[node.id]
+        if node.id in sums:               # the sum itself
+            pid, write, make = sums[node.id]
             if not write:
-                launches.append(_colsum_launch(graph, graph.nodes[pid], node, False))
+                launches.append(make(graph, graph.nodes[pid], node, False))
             continue
         ops = _matmul_operands(graph, node) if folds else None
         if ops and set(ops) & folds:

@@ -903,7 +903,7 @@ static std::pair<i64, i64> splitk_plan(i64 batch, i64 M, i64 K, i64 N, i64 bn, s
   i64 kb = kpad(K) / 32;
   i64 s = 1;
   if (tiles < SM_COUNT && SM_COUNT / tiles > 8 && kb >= 8) {
-    s = std::max<i64>(1, std::min({(i64)SM_COUNT / tiles, kb / 4, (i64)64}));
+    s = std::max<i64>(1, std::min<i64>((i64)SM_COUNT / tiles, kb / 4));
     s = cdiv(kb, cdiv(kb, s));
   }
   return {s, split_bytes(batch, M, K, N, fs) + 256};
@@ -1376,6 +1376,74 @@ static Launch colsum_launch(const Graph& g, const Node& P, const Node& S, bool w
   return l;
 }
 
+// ---------------------------------------------------------------- elementwise + row sum
+static const i64 ROWSUM_MIN_ROWS = (i64)SM_COUNT * 8;
+
+static std::map<int, std::pair<int, bool>> rowsum_fusions(const Graph& g, const std::set<int>& keep,
+                                                          const std::set<int>& exclude) {
+  std::map<int, std::vector<int>> consumers;
+  for (auto& n : g.nodes)
+    for (int i : n.inputs) consumers[i].push_back(n.id);
+  std::map<int, std::pair<int, bool>> out;
+  std::set<int> taken;
+  for (auto& S : g.nodes) {
+    if (S.op != "sum" || exclude.count(S.id)) continue;
+    const Node& P = g.nodes[S.inputs[0]];
+    if (P.shape.size() < 2 || S.axis != (int)P.shape.size() - 1 || taken.count(P.id) || exclude.count(P.id) ||
+        size_of(std::vector<i64>(P.shape.begin(), P.shape.end() - 1)) < ROWSUM_MIN_ROWS || !elementwise_producer(P))
+      continue;
+    out[S.id] = {P.id, keep.count(P.id) > 0 || consumers[P.id].size() > 1};
+    taken.insert(P.id);
+  }
+  return out;
+}
+
+static Launch rowsum_launch(const Graph& g, const Node& P, const Node& S, bool write) {
+  std::shared_ptr<Graph> owned;
+  const Graph* body;
+  int out_id;
+  if (P.op == "fused") {
+    body = P.body.get();
+    out_id = P.output;
+  } else {
+    std::vector<std::vector<i64>> shapes;
+    for (int i : P.inputs) shapes.push_back(g.nodes[i].shape);
+    owned = one_op_body(P, shapes, &out_id);
+    body = owned.get();
+  }
+  i64 R = size_of(std::vector<i64>(P.shape.begin(), P.shape.end() - 1)), C = P.shape.back();
+  Launch l;
+  l.code = "// elementwise (" + P.op + ") + sum over the last axis of [" + std::to_string(R) + ", " + std::to_string(C) +
+           "], value " + (write ? "stored" : "not stored") + "\n"
+           "#include \"tcb/common.cuh\"\n"
+           "#define TCB_OUTER " + std::to_string(R) + "\n"
+           "#define TCB_N " + std::to_string(C) + "\n"
+           "#define TCB_INNER 1\n"
+           "#define TCB_SPLIT 1\n"
+           "#define TCB_IS_MAX 0\n"
+           "#define TCB_WRITE " + std::to_string((int)write) + "\n" +
+           ew_body_struct(*body, out_id, R * C) + "#include \"tcb/rowsum.cuh\"\n";
+  Call main = make_call("tcb_ew_rowsum", {std::max<i64>(1, std::min<i64>(cdiv(R * 32, 256), SM_COUNT * 8)), 1, 1},
+                        {256, 1, 1});
+  if (write) main.ptr_params = {{14, S.id}};
+  l.calls.push_back(main);
+  l.node = write ? P.id : S.id;
+  l.op = "fused";
+  l.kind = "fused-rowsum";
+  l.pattern = "elementwise+rowsum";
+  l.has_pattern = true;
+  l.inputs = P.inputs;
+  l.scratch_bytes = 0;
+  l.info = {{"R", num(R)}, {"C", num(C)}, {"write", boolean(write)}, {"producer", num(P.id)}, {"sum", num(S.id)}};
+  if (write) l.nodes = {P.id, S.id};
+  std::set<int> seen;
+  i64 nb = 0;
+  for (int i : P.inputs)
+    if (seen.insert(i).second) nb += size_of(g.nodes[i].shape) * 4;
+  l.bytes = nb + R * 4 + (write ? R * C * 4 : 0);
+  return l;
+}
+
 // ---------------------------------------------------------------- one pass, several elementwise outputs
 static bool reads_directly(const Node& node, int k) {
   if (node.op != "fused") return true;
@@ -1565,12 +1633,22 @@ static void lower_graph(Lowering& L, const Options& o) {
   std::set<int> folds = o.fold ? foldable_transposes(g, o.matmul, o.keep) : std::set<int>();
   std::map<int, std::pair<int, bool>> cols = (o.fused && o.colfuse) ? colsum_fusions(g, o.keep)
                                                                      : std::map<int, std::pair<int, bool>>();
-  std::map<int, std::pair<int, bool>> producer_of;
-  for (auto& [sid, pw] : cols) producer_of[pw.first] = {sid, pw.second};
+  std::map<int, std::pair<int, bool>> rows;
+  if (o.fused && o.colfuse) {
+    std::set<int> taken;
+    for (auto& [sid, pw] : cols) { taken.insert(sid); taken.insert(pw.first); }
+    rows = rowsum_fusions(g, o.keep, taken);
+  }
+  // sum id -> (producer id, write, row sum?)
+  std::map<int, std::tuple<int, bool, bool>> sums;
+  for (auto& [sid, pw] : cols) sums[sid] = {pw.first, pw.second, false};
+  for (auto& [sid, pw] : rows) sums[sid] = {pw.first, pw.second, true};
+  std::map<int, std::tuple<int, bool, bool>> producer_of;
+  for (auto& [sid, t] : sums) producer_of[std::get<0>(t)] = {sid, std::get<1>(t), std::get<2>(t)};
   std::map<int, int> mos;
   if (o.fused && o.mofuse) {
     std::set<int> exclude(folds.begin(), folds.end());
-    for (auto& kv : cols) exclude.insert(kv.first);
+    for (auto& kv : sums) exclude.insert(kv.first);
     for (auto& kv : producer_of) exclude.insert(kv.first);
     mos = mo_fusions(g, o.keep, exclude);
   }
@@ -1583,13 +1661,13 @@ static void lower_graph(Lowering& L, const Options& o) {
       continue;
     }
     if (producer_of.count(node.id)) {
-      auto [sid, write] = producer_of[node.id];
-      if (write) L.launches.push_back(colsum_launch(g, node, g.nodes[sid], true));
+      auto [sid, write, row] = producer_of[node.id];
+      if (write) L.launches.push_back(row ? rowsum_launch(g, node, g.nodes[sid], true) : colsum_launch(g, node, g.nodes[sid], true));
       continue;
     }
-    if (cols.count(node.id)) {
-      auto [pid, write] = cols[node.id];
-      if (!write) L.launches.push_back(colsum_launch(g, g.nodes[pid], node, false));
+    if (sums.count(node.id)) {
+      auto [pid, write, row] = sums[node.id];
+      if (!write) L.launches.push_back(row ? rowsum_launch(g, g.nodes[pid], node, false) : colsum_launch(g, g.nodes[pid], node, false));
       continue;
     }
     std::pair<int, int> ab;
