@@ -771,6 +771,16 @@ def c5_record(args, runner, world, rank, local):
     if comm:
         comm.wait()
     e2e_ms = _max_over_ranks(e2e_total / ke, world)
+    coll_ms = None
+    if comm:
+        # the whole flat gradient buffer reduced alone, every rank the same calls: what the collective
+        # would cost the step if nothing overlapped it
+        def ar(k, ev):
+            comm.allreduce_mean(tr.flat.ptr, tr.flat_floats, prescaled=tr.prescaled)
+        ar_total, ev3, _ = _timed(runner, rt, world, local, 10, 3, ar)
+        ev3.free()
+        comm.wait()
+        coll_ms = _max_over_ranks(ar_total / 10, world)
     rec = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": Wm,
         "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -792,6 +802,15 @@ def c5_record(args, runner, world, rank, local):
         "gpu_launches": K * tr.kernel_launches,
         "clocks": clk,
     }
+    gap = ms - sr["ideal_ms"]
+    if coll_ms is not None:
+        rec["collective"] = {"allreduce_alone_ms": round(coll_ms, 3), "bytes": tr.flat_floats * 4,
+                             "buckets": len(tr.bucket_spans) if tr.buckets > 1 else 1}
+    rec["limiter"] = (f"per-rank kernels: the step takes {ms:.3f} ms against {sr['ideal_ms']:.3f} ms with every "
+                      f"launch at its own roofline ({gap:.3f} ms above it, {tr.kernel_launches} launches)"
+                      + (f"; the gradient allreduce alone takes {coll_ms:.3f} ms, "
+                         + (f"{len(tr.bucket_spans) - 1} of its {len(tr.bucket_spans)} buckets overlapping the "
+                            f"backward" if tr.buckets > 1 else "after the backward") if coll_ms is not None else ""))
     if rank == 0 and world == 1 and not args.no_cpu:
         oracle = _oracle()
         graph, inputs, units = cpu_sample("c5", wl, pkg, cg, 1)

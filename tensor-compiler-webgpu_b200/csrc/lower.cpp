@@ -44,7 +44,7 @@ constexpr i64 SMEM_LIMIT = 227 * 1024;
 constexpr i64 KPAD = 32;
 constexpr i64 TMA_ATOM32 = (i64)1 << 32;
 constexpr i64 GEMM_STAGING = 4 * 2 * 32 * 32 * 4;
-constexpr int FS_MAX_REREAD = 4;
+constexpr int FS_MAX_REREAD = 8;
 
 struct Error : std::runtime_error {
   using std::runtime_error::runtime_error;

@@ -57,11 +57,12 @@ extern "C" __global__ void __launch_bounds__(256) tcb_reduce_cols(const tcb::Arg
     const float* p = x + (o * (u64)TCB_N) * (u64)TCB_INNER + j;
     float acc = tcb::red_init();
     u64 k = k0;
-    for (; k + 4 <= k1; k += 4) {  // four independent loads in flight
-      float v0 = __ldg(p + (k + 0) * (u64)TCB_INNER), v1 = __ldg(p + (k + 1) * (u64)TCB_INNER);
-      float v2 = __ldg(p + (k + 2) * (u64)TCB_INNER), v3 = __ldg(p + (k + 3) * (u64)TCB_INNER);
-      acc = tcb::red_comb(acc, v0); acc = tcb::red_comb(acc, v1);
-      acc = tcb::red_comb(acc, v2); acc = tcb::red_comb(acc, v3);
+    for (; k + 8 <= k1; k += 8) {  // eight independent loads in flight, combined in row order
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(p + (k + u) * (u64)TCB_INNER);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = tcb::red_comb(acc, v[u]);
     }
     for (; k < k1; ++k) acc = tcb::red_comb(acc, __ldg(p + k * (u64)TCB_INNER));
     dst[s * outs + i] = acc;

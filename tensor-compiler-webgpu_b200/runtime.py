@@ -518,8 +518,17 @@ class MultiLaunch:
         self.bytes = sum(m.bytes for m in members)
         self.info = {"members": len(members)}
         c = m0.calls[0]
-        gx = max(m.calls[0].grid[0] for m in members)   # the grid-stride loop covers every member's count
+        # the grid-stride loop covers every member's count: about one wave of CTAs over all members
+        gx = min(max(m.calls[0].grid[0] for m in members), one_wave_share(len(members)))
         self.calls = [KernelCall("tcb_elementwise_multi", (gx, len(members), 1), c.block, c.smem, c.params)]
+
+
+def one_wave_share(members, ctas_per_sm=8):
+    """x-extent of a (gx, members) grid whose members each grid-stride over their own work: about one
+    wave of CTAs in all.  Sizing every member for the largest one's count made tens of thousands of
+    CTAs, most exiting at once (C5's weight split: 56 us for 13 MB)."""
+    from .codegen import SM_COUNT
+    return max(1, -(-SM_COUNT * ctas_per_sm // max(1, members)))
 
 
 def batch_small_launches(launches, root, max_elems=BATCH_MAX_ELEMS):
@@ -779,6 +788,7 @@ class Program:
         gx = 1
         for src, hi, lo, b, R, C, kp, cols in jobs:
             gx = max(gx, grid1d(b * R * kp, per_thread=1)[0] if not cols else min(b * (kp // 32) * -(-R // 32), 148 * 8))
+        gx = min(gx, one_wave_share(len(jobs)))   # every job grid-strides: about one wave of CTAs in all
         mod = self.runner.pipeline(split_multi_source())
         self._hoist = (KernelCall("tcb_split_multi", (gx, len(jobs), 1), (256, 1, 1), 0, []), mod, tbuf.ptr)
         issue(self._hoist[0], mod, [], 0, tbuf.ptr, plan=plan)
@@ -800,7 +810,7 @@ class Program:
             buf = DeviceBuffer(self.runner, ctypes.sizeof(table))
             check(lib().tc_upload(buf.handle, ctypes.addressof(table), ctypes.sizeof(table), 0))
             self.tables.append(buf)
-            gx = max(grid1d(n, per_thread=w)[0] for _, _, n in items)
+            gx = min(max(grid1d(n, per_thread=w)[0] for _, _, n in items), one_wave_share(len(items)))
             issue(KernelCall("tcb_elementwise_multi", (gx, len(items), 1), (WG, 1, 1), 0, [0]), mod, [], 0, buf.ptr,
                   plan=plan)
         return len(by_w)
