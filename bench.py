@@ -15,8 +15,9 @@ The rest of the metric rides in `records`, each with its own roofline, clocks, e
   c3 -- the matmul + bias + relu/tanh on the tcgen05 3xTF32 path, both BASELINE shapes (TFLOP/s);
   c4 -- softmax and logSoftmax forward + backward on [65536, 4096], 1 % of rows +800 (GB/s);
   train -- the C5 decoder transformer's training step (tokens/s), data parallel over every rank:
-           each rank runs its shard of the global batch 512, one NCCL allreduce of the gradients
-           (the library's own communicator) between the gradient and Adam programs.
+           each rank runs its shard of the global batch 512; the gradients are sum-allreduced over NCCL
+           (the library's own communicator) in buckets on a collective stream during the backward,
+           and every rank runs the same Adam program.
 With --gpus N (one process per GPU, torchrun), C2 runs as N replicas (no data-path collective, `scaling`
 weak) and `train` runs the global batch over the N ranks (strong scaling); c1/c3/c4 are 1-GPU records.
 
@@ -720,8 +721,9 @@ def _collective(tr, world):
 
 def c5_record(args, runner, world, rank, local):
     """C5: the decoder transformer's training step, data parallel over the batch (tokens/s): every rank
-    runs the gradient program on its shard, the library's NCCL communicator sums the gradients (one
-    allreduce of one flat buffer), every rank runs the same Adam program."""
+    runs the gradient program on its shard, the library's NCCL communicator sums the gradients (the
+    flat gradient buffer in buckets, each reduced as soon as the backward has written it), every rank
+    runs the same Adam program."""
     pkg, rt, cg, wl = _mods()
     dp = importlib.import_module(PKG + ".dp")
     cfg, c = wl.c5_cfg(batch=args.batch or wl.C5_CONFIG["batch"])

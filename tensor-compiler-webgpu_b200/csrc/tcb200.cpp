@@ -645,11 +645,12 @@ struct tc_plan {
     CUevent ready = nullptr;  // an allreduce: recorded on the plan's stream, waited for by the collective stream
   };
   std::vector<Entry> entries;
-  // Programmatic dependent launch between consecutive template kernels: $TCB_PDL=0 never, 1 always, unset
-  // (the default) only where both grids fit in one wave (at most one CTA per SM).  Measured on the B200: a
-  // chain of one-wave kernels (the C1 step) gains 9 %; the transformer step, whose kernels fill the GPU,
-  // loses 6 % with every edge programmatic.
-  int pdl = 2;
+  // Programmatic dependent launch between consecutive template kernels: $TCB_PDL=0 never, 1 always, 2 where
+  // both grids fit in one wave (at most one CTA per SM), unset (the default, 3) where the kernel being
+  // launched fits in one wave.  Measured on the B200: a chain of one-wave kernels (the C1 step) gains 9 %;
+  // the transformer step, whose elementwise kernels fill the GPU, loses 6 % with every edge programmatic,
+  // and gains 0.8 % at 64 sequences when its one-wave GEMMs start their set-up under the previous tail.
+  int pdl = 3;
   // Captured form: one graph per segment between allreduce entries (a collective is never captured; it is
   // enqueued between the segments' graph launches).  Empty segments have none.
   bool captured = false;
@@ -668,7 +669,7 @@ int tc_plan_create(tc_ctx* ctx, tc_plan** out) {
   *out = new tc_plan();
   (*out)->ctx = ctx;
   const char* e = getenv("TCB_PDL");
-  (*out)->pdl = e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : 2;
+  (*out)->pdl = e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : e && e[0] == '2' ? 2 : 3;
   return TC_OK;
 }
 
@@ -755,7 +756,8 @@ static int plan_issue(tc_plan* plan, size_t b, size_t end, CUstream st) {
       continue;
     }
     const uint64_t ctas = (uint64_t)e.grid[0] * e.grid[1] * e.grid[2];
-    const bool pdl = plan->pdl == 1 || (plan->pdl == 2 && ctas <= wave && prev_ctas <= wave);
+    const bool pdl = plan->pdl == 1 || (plan->pdl == 2 && ctas <= wave && prev_ctas <= wave) ||
+                     (plan->pdl == 3 && ctas <= wave);
     prev_ctas = ctas;
     void* params[1];
     tc_args a = e.args;

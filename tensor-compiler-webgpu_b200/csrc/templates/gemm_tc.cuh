@@ -324,7 +324,6 @@ extern "C" __global__ void __launch_bounds__(128) tcb_gemm_prep(const tcb::Args 
 extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192, 1)
     tcb_gemm_tc(const __grid_constant__ tcb::GemmParams P) {
   using namespace tcb;
-  grid_dependency_sync();
   using S = GemmShape;
   constexpr int BN = TCB_BN, STAGES = TCB_STAGES;
   constexpr bool FA = TCB_FS_A != 0, FB = TCB_FS_B != 0, FS = FA || FB;
@@ -337,6 +336,7 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
   extern __shared__ unsigned char smem_raw[];
   u32* err = reinterpret_cast<u32*>(P.a.p[15]);  // global error word (may be null)
   if (gridDim.x != S::GRID) {                     // the unit schedule assumes exactly GRID CTAs
+    grid_dependency_sync();
     if (threadIdx.x == 0 && err) atomicCAS(err, 0u, 9u);
     return;
   }
@@ -401,6 +401,9 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
   __syncthreads();
   tc_fence_after();
   const u32 tmem = *tmem_slot;
+  // the set-up above touches only this CTA's shared and tensor memory, so it may overlap the previous
+  // kernel's tail (programmatic dependent launch); every global access comes after this wait
+  grid_dependency_sync();
 
   if (warp == 0) {
     if (lane == 0) {
