@@ -24,6 +24,36 @@ extern "C" __global__ void __launch_bounds__(256) tcb_reduce_rows(const tcb::Arg
   const u64 warp = ((u64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const u64 warps = ((u64)gridDim.x * blockDim.x) >> 5;
   const int lane = threadIdx.x & 31;
+  if constexpr ((u64)TCB_OUTER <= 8 && TCB_N >= 1024) {
+    // at most 8 long rows (a loss summed over every token): the launch is one CTA, and its 8 warps share
+    // each row -- thread t takes 4 consecutive values (1 when the row length is not a multiple of 4)
+    // every 256, its warp sums, then warp 0 combines the 8 warp sums in warp order
+    __shared__ float part[8];
+    constexpr int W = TCB_N % 4 == 0 ? 4 : 1;
+    for (u64 o = 0; o < (u64)TCB_OUTER; ++o) {
+      const float* row = x + o * (u64)TCB_N;
+      float acc = tcb::red_init();
+      for (u64 k = threadIdx.x; k < (u64)TCB_N / W; k += blockDim.x) {
+        if constexpr (W == 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(row) + k);
+          acc = tcb::red_comb(acc, v.x); acc = tcb::red_comb(acc, v.y);
+          acc = tcb::red_comb(acc, v.z); acc = tcb::red_comb(acc, v.w);
+        } else {
+          acc = tcb::red_comb(acc, __ldg(row + k));
+        }
+      }
+      acc = TCB_IS_MAX ? tcb::warp_max(acc) : tcb::warp_sum(acc);
+      if (lane == 0) part[threadIdx.x >> 5] = acc;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float s = part[0];
+        for (unsigned w = 1; w < blockDim.x / 32; ++w) s = tcb::red_comb(s, part[w]);
+        out[o] = s;
+      }
+      __syncthreads();
+    }
+    return;
+  }
   for (u64 o = warp; o < (u64)TCB_OUTER; o += warps) {
     const float* row = x + o * (u64)TCB_N;
     float acc = tcb::red_init();
