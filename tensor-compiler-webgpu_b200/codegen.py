@@ -738,12 +738,17 @@ def ctrl_bytes(rem):
     return (16 + 16 * rem + 63) // 64 * 64
 
 
+TAIL_MIN_KB = 32   # a last wave is split along K only with at least this many K-blocks: for K = 256 (16 blocks)
+#                    the partial tiles' write and re-read cost more than the fuller wave gains (16384 x 256 x
+#                    1024: 67.4 us split, 50.0 not; 4096^3: 602 split, 636 not)
+
+
 def tail_plan(batch, M, K, N, bn, bk, splitk, fs=(False, False)):
     """The persistent GEMM's grid and K-range split of the tiles of its last wave.
 
     Returns (grid, tail, rem, tail_off, scratch_end).  grid = min(SMs, tiles) CTAs; when the last wave
-    would hold rem <= grid/2 tiles, each of them is cut into `tail` K ranges (>= 4 k-blocks each, at
-    most 8) so that wave fills the SMs.  With fewer tiles than SMs that is every tile: grid becomes
+    would hold rem <= grid/2 tiles and K has at least TAIL_MIN_KB k-blocks, each of them is cut into
+    `tail` K ranges (>= 4 k-blocks each, at most 8) so that wave fills the SMs.  With fewer tiles than SMs that is every tile: grid becomes
     tiles x tail, one range per CTA.  The ranges' partial tiles (128 x bn floats each) sit at tail_off
     in scratch, after the control block; scratch_end is the end of that region (0 when nothing is split).
     """
@@ -758,7 +763,7 @@ def tail_plan(batch, M, K, N, bn, bk, splitk, fs=(False, False)):
         grid = min(SM_COUNT, tiles)
         rem = tiles % grid
         tail = 1
-        if splitk == 1 and rem and 2 * rem <= grid:
+        if splitk == 1 and rem and 2 * rem <= grid and kbs >= TAIL_MIN_KB:
             tail = min(grid // rem, kbs // 4, 8)
         if tail < 2:
             return grid, 1, 0, 0, 0

@@ -45,6 +45,7 @@ constexpr i64 KPAD = 32;
 constexpr i64 TMA_ATOM32 = (i64)1 << 32;
 constexpr i64 GEMM_STAGING = 4 * 2 * 32 * 32 * 4;
 constexpr int FS_MAX_REREAD = 8;
+constexpr i64 TAIL_MIN_KB = 32;
 
 struct Error : std::runtime_error {
   using std::runtime_error::runtime_error;
@@ -927,7 +928,7 @@ static TailPlan tail_plan(i64 batch, i64 M, i64 K, i64 N, i64 bn, i64 bk, i64 sp
     grid = std::min<i64>(SM_COUNT, tiles);
     rem = tiles % grid;
     tail = 1;
-    if (splitk == 1 && rem && 2 * rem <= grid) tail = std::min<i64>({grid / rem, kbs / 4, (i64)8});
+    if (splitk == 1 && rem && 2 * rem <= grid && kbs >= TAIL_MIN_KB) tail = std::min<i64>({grid / rem, kbs / 4, (i64)8});
     if (tail < 2) return {grid, 1, 0, 0, 0};
   }
   i64 tail_off = split_bytes(batch, M, K, N, fs) + std::max<i64>(256, (ctrl_bytes(rem) + 255) / 256 * 256);

@@ -114,11 +114,12 @@ extern "C" __global__ void __launch_bounds__(256) tcb_reduce_finish(const tcb::A
     float acc = tcb::red_init();
     if (i < outs) {
       int s = w;
-      for (; s + 24 < TCB_SPLIT; s += 32) {  // four independent loads in flight
-        const float v0 = part[(u64)s * outs + i], v1 = part[(u64)(s + 8) * outs + i];
-        const float v2 = part[(u64)(s + 16) * outs + i], v3 = part[(u64)(s + 24) * outs + i];
-        acc = tcb::red_comb(acc, v0); acc = tcb::red_comb(acc, v1);
-        acc = tcb::red_comb(acc, v2); acc = tcb::red_comb(acc, v3);
+      for (; s + 56 < TCB_SPLIT; s += 64) {  // eight independent loads in flight, combined in chunk order
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = part[(u64)(s + 8 * u) * outs + i];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc = tcb::red_comb(acc, v[u]);
       }
       for (; s < TCB_SPLIT; s += 8) acc = tcb::red_comb(acc, part[(u64)s * outs + i]);
     }

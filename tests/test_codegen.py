@@ -107,7 +107,8 @@ def test_transpose_folding_picks_only_gemm_operand_transposes(pkg, cg):
 @pytest.mark.parametrize("shape", [(1, 4096, 4096, 4096), (1, 16384, 1024, 4096), (198, 128, 256, 128),
                                    (1, 5120, 256, 1024), (1, 2432, 128, 2048), (2048, 256, 64, 256),
                                    (1, 256, 131072, 768), (3, 300, 96, 500), (1, 16384, 256, 256),
-                                   (1, 2560, 1024, 512), (1, 256, 16384, 1024)])
+                                   (1, 2560, 1024, 512), (1, 256, 16384, 1024), (1, 3456, 512, 2048),
+                                   (1, 5760, 512, 1024), (1, 16384, 256, 1024), (256, 256, 256, 64)])
 def test_gemm_last_wave_plan(cg, shape):
     """The persistent GEMM's unit schedule: every (tile, k-block) is covered exactly once, the last wave
     is split only when it would leave at least half the CTAs idle, and no CTA gets more than one
@@ -147,6 +148,11 @@ def test_gemm_last_wave_plan(cg, shape):
         assert splitk == 1 and 2 * rem <= grid and kb_all // tail >= 4
         assert rem_plan == rem and tail_off >= cg.ctrl_bytes(rem)
         assert end == tail_off + rem * tail * cg.GEMM_BM * bn * 4
+        if tiles >= cg.SM_COUNT:
+            assert kb_all >= cg.TAIL_MIN_KB        # a last wave is split only with a long enough K
+    elif tiles >= cg.SM_COUNT and splitk == 1:
+        r = tiles % grid
+        assert not (r and 2 * r <= grid and kb_all >= cg.TAIL_MIN_KB and min(grid // r, kb_all // 4, 8) >= 2)
 
 
 def test_batch_small_launches_keeps_dependencies():

@@ -69,7 +69,7 @@ def test_c3_matmul_epilogue(pkg, oracle, runner, wl, cg, M, K, N, act):
         assert j["pass"], (matmul, j)
 
 
-@pytest.mark.parametrize("M,K,N,tail", [(2432, 128, 2048, 2), (5120, 256, 1024, 4)])
+@pytest.mark.parametrize("M,K,N,tail", [(3456, 512, 2048, 2), (5760, 512, 1024, 4)])
 def test_c3_last_wave_split(pkg, oracle, runner, wl, cg, M, K, N, tail):
     """Shapes whose last wave of output tiles is cut into K ranges (reduced by the last arriver):
     judged against the oracle, and bitwise the same on a second run."""
@@ -156,12 +156,12 @@ def test_gemm_operand_layouts(pkg, oracle, runner, wl, cg, monkeypatch, a_t, b_t
 
 @pytest.mark.parametrize("a_t,b_t", [(False, False), (True, True)])
 def test_gemm_last_wave_split_with_in_kernel_operand_split(pkg, oracle, runner, cg, a_t, b_t):
-    """150 batched 128 x 256 x 64 products: 150 tiles on 148 CTAs, so the last two tiles are cut into K
-    ranges, while both operands are split inside the GEMM (each is loaded by one tile): judged against
-    the oracle."""
+    """150 batched 128 x 1024 x 64 products: 150 tiles on 148 CTAs, so the last two tiles are cut into K
+    ranges (K has 32 K-blocks: long enough to split), while both operands are split inside the GEMM
+    (each is loaded by one tile): judged against the oracle."""
     from importlib import import_module
     ir = import_module("tensor-compiler-webgpu_b200.ir")
-    Bt, M, K, N = 150, 128, 256, 64
+    Bt, M, K, N = 150, 128, 1024, 64
     g = ir.Graph()
     x = g.input("x", [Bt, K, M] if a_t else [Bt, M, K])
     y = g.input("y", [Bt, N, K] if b_t else [Bt, K, N])
