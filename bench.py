@@ -838,8 +838,9 @@ def c1_record(args, runner, rank):
     inputs[step["cotangent"]] = [1.0]
     keep = [step["loss"], *step["outputs"].values()]
     fused = pkg.fuse.fuse(step["graph"], keep=keep)
-    lowered = cg.lower_fused(fused.graph, matmul="naive")
     outs = [fused.index[k] for k in dict.fromkeys(keep)]
+    # the trainers' resident lowering: sums and elementwise readers in their producers' passes
+    lowered = cg.lower_fused(fused.graph, matmul="naive", colfuse=True, mofuse=True, keep=outs)
     prog = rt.Program(runner, fused.graph, lowered, keep=outs)
     name_of = {n.id: n.attrs["name"] for n in fused.graph.nodes if n.op == "input"}
     for nid, nm in name_of.items():

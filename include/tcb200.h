@@ -167,8 +167,10 @@ int tc_plan_memory(int n, const uint64_t* bytes, const int32_t* first_use, const
  *      the fusion pass's fused nodes (attrs {kind, pattern, body, output}, src/fusion/fuse.js:278-279).
  *      `opts_json` (NULL = defaults): {"fused": true (lowerFused; false: lower), "matmul": "naive" |
  *      "tiled" (the tcgen05 3xTF32 GEMM where K >= 32), "sabotage": one of the reference's
- *      FUSED_SABOTAGE names or null, "fold": false (transposes read only as GEMM operands get no launch),
- *      "colfuse": false (sums over axis 0 run inside their elementwise producer), "mofuse": false (an
+ *      FUSED_SABOTAGE names or null, "fold": false (transposes read only as GEMM operands get no launch,
+ *      and a GEMM read only by a transpose computes the transposed product in its place),
+ *      "colfuse": false (sums over axis 0, and over the last axis of at least 1184 rows, run inside
+ *      their elementwise producer), "mofuse": false (an
  *      elementwise reader whose other operands already exist is computed in its elementwise producer's
  *      pass, both stored), "keep": [node ids that must exist after the launches]}.  No device is needed.  Each launch's CUDA source, kernel calls
  *      (grid, block, shared memory, parameters, tensor maps, error word) and scratch are those the
@@ -178,7 +180,8 @@ int tc_lower_json(const char* graph_json, const char* opts_json, tc_lowered** ou
 int tc_lowered_count(tc_lowered* l, int* n);
 /* The launch records as JSON ({"launches": [{node, nodes?, op, kind, pattern, inputs, code, scratch_bytes,
  * bytes, calls: [{name, grid, block, smem, params, err_offset, out_node, ptr_params, tma}], info}],
- * "folded": [...]}, the reference's {node, op, kind, pattern, inputs, params, grid, code} record,
+ * "folded": [...], "transposed": [[transpose id, matmul id], ...]}, the reference's {node, op, kind,
+ * pattern, inputs, params, grid, code} record,
  * src/gpu/lower.js:108-111) into `json` (cap bytes); *needed = its size with the NUL.  json may be NULL. */
 int tc_lowered_json(tc_lowered* l, char* json, uint64_t cap, uint64_t* needed);
 int tc_lowered_free(tc_lowered* l);

@@ -592,7 +592,7 @@ def _row_value(em, nid):
 
 
 # ------------------------------------------------------------------ matmul epilogue
-def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=False, b_t=False):
+def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=False, b_t=False, cross_ba=False):
     root = next(n for n in body.nodes if n.op == "matmul")
     ia, ib = (int(body.nodes[i].attrs["name"][1:]) for i in root.inputs)
     a_s, b_s = body.nodes[root.inputs[0]].shape, body.nodes[root.inputs[1]].shape
@@ -643,7 +643,8 @@ def _epilogue_source(body, out_id, sabotage=None, kernel="simt", bn=None, a_t=Fa
                    f"#define TCB_SPLITK {splitk}\n#define TCB_PART_OFFSET {part_off}ull\n"
                    f"#define TCB_GRID {grid}\n#define TCB_TAIL_SPLIT {tail}\n"
                    f"#define TCB_TAIL_OFFSET {tail_off}ull\n"
-                   f"#define TCB_A_T {int(a_t)}\n#define TCB_B_T {int(b_t)}\n")
+                   f"#define TCB_A_T {int(a_t)}\n#define TCB_B_T {int(b_t)}\n"
+                   + ("#define TCB_CROSS_BA 1\n" if cross_ba else ""))
     src = f"""// matmul epilogue ({kernel}): batch {batch}, [{M},{K}] x [{K},{N}]
 #include "tcb/common.cuh"
 #define TCB_M {M}
@@ -810,11 +811,13 @@ def gemm_bn(N):
     return 256 if N >= 256 else 64 if N <= 64 else 128
 
 
-def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage=None, a_t=False, b_t=False):
+def _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage=None, a_t=False, b_t=False,
+                        cross_ba=False):
     root = next(n for n in body.nodes if n.op == "matmul")
     N = body.nodes[root.inputs[1]].shape[-1]
     bn = gemm_bn(N)
-    code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage, kernel="tcgen05", bn=bn, a_t=a_t, b_t=b_t)
+    code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage, kernel="tcgen05", bn=bn, a_t=a_t, b_t=b_t,
+                                              cross_ba=cross_ba)
     if batch > 65535 or math.ceil(M / GEMM_BM) > 65535:
         raise ValueError("matmul grid too large")
     Kp = _kpad(K)
@@ -983,14 +986,17 @@ def uses_tensor_cores(a_shape, matmul):
     return matmul == "tiled" and a_shape[-1] >= TC_MIN_K
 
 
-def _epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, matmul, sabotage=None, a_t=False, b_t=False):
+def _epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, matmul, sabotage=None, a_t=False, b_t=False,
+                     cross_ba=False):
     """`matmul`: 'naive' -> the CUDA-core fp32 kernel; 'tiled' -> tcgen05 3xTF32 when K >= TC_MIN_K.
 
     `a_t` / `b_t`: the operand's slot holds its transpose (a folded transposeLast2, tensor-core path only).
+    `cross_ba`: issue the two mixed 3xTF32 products as A_hi.B_lo then A_lo.B_hi (a transposed product
+    computing (A.B)^T = B^T.A^T adds its terms in the order A.B would).
     """
     root = next(n for n in body.nodes if n.op == "matmul")
     if uses_tensor_cores(body.nodes[root.inputs[0]].shape, matmul):
-        return _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage, a_t, b_t)
+        return _tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage, a_t, b_t, cross_ba)
     if a_t or b_t:
         raise ValueError("transposed operands are folded only on the tensor-core path")
     code, (batch, M, K, N) = _epilogue_source(body, out_id, sabotage)
@@ -1157,12 +1163,57 @@ def _folded_launch(graph, node, matmul, sabotage, folds):
     return lau
 
 
+def transposed_products(graph, matmul, keep=(), folds=()):
+    """{transposeLast2 id: matmul id} for a plain tensor-core matmul C = A.B whose only reader is a
+    transposeLast2 that does not itself fold into a GEMM: the pair becomes one GEMM computing
+    C^T = B^T.A^T directly -- no transpose pass over C, and when C has few rows (attention's
+    [64, 256] products of a head dimension of 64) no 128-row tile half spent on padding.  Autodiff
+    makes these: the gradient of K^T's reader, transposed back."""
+    keep, folds = set(keep), set(folds)
+    consumers = {}
+    for n in graph.nodes:
+        for i in n.inputs:
+            consumers.setdefault(i, []).append(n.id)
+    out = {}
+    for T in graph.nodes:
+        if T.op != "transpose" or not _is_last2_swap(T) or T.id in folds:
+            continue
+        M = graph.nodes[T.inputs[0]]
+        if (M.op != "matmul" or M.id in keep or consumers.get(M.id) != [T.id]
+                or not uses_tensor_cores(graph.nodes[M.inputs[0]].shape, matmul)):
+            continue
+        out[T.id] = M.id
+    return out
+
+
+def _transposed_product_launch(graph, T, M, matmul, folds):
+    """The GEMM launch of node T = transpose(M), M = A.B: T = B^T.A^T, each operand read through its
+    folded transposes with the swapped flag (the slot of B^T holds B's source, transposed when B is
+    not itself a transpose, and likewise for A^T)."""
+    a_src, a_t = _unfold(graph, M.inputs[0], folds)
+    b_src, b_t = _unfold(graph, M.inputs[1], folds)
+    sa, sb = list(graph.nodes[M.inputs[0]].shape), list(graph.nodes[M.inputs[1]].shape)
+    shapes = [sb[:-2] + [sb[-1], sb[-2]], sa[:-2] + [sa[-1], sa[-2]]]
+    body, out = _one_op_body("matmul", shapes, M.attrs)
+    lau = _epilogue_launch(body, out, T.id, "matmul", f"matmul-{matmul}", None, [b_src, a_src], matmul, None,
+                           not b_t, not a_t, cross_ba=True)
+    lau.inputs = [b_src, a_src]
+    lau.bytes = _bytes(graph, lau)
+    return lau
+
+
 def lower(graph, matmul="naive", sabotage=None, fold=False, keep=()):
-    """One launch per op, no fusion (src/gpu/lower.js:68-114).  `fold`: drop transposes feeding GEMM operands."""
+    """One launch per op, no fusion (src/gpu/lower.js:68-114).  `fold`: drop transposes feeding GEMM
+    operands, and compute a GEMM read only by a transpose as the transposed product."""
     folds = foldable_transposes(graph, matmul, keep) if fold else set()
+    tprods = transposed_products(graph, matmul, keep, folds) if fold else {}
+    tmats = set(tprods.values())
     launches = []
     for node in graph.nodes:
-        if node.op in ("input", "const") or node.id in folds:
+        if node.op in ("input", "const") or node.id in folds or node.id in tmats:
+            continue
+        if node.id in tprods:
+            launches.append(_transposed_product_launch(graph, node, graph.nodes[tprods[node.id]], matmul, folds))
             continue
         if folds and _matmul_operands(graph, node) and set(_matmul_operands(graph, node)) & folds:
             lau = _folded_launch(graph, node, matmul, sabotage, folds)
@@ -1170,7 +1221,7 @@ def lower(graph, matmul="naive", sabotage=None, fold=False, keep=()):
             lau = _plain_launch(graph, node, matmul)
         lau.bytes = _bytes(graph, lau)
         launches.append(lau)
-    return {"launches": launches, "folded": sorted(folds)}
+    return {"launches": launches, "folded": sorted(folds), "transposed": sorted(tprods.items())}
 
 
 # ------------------------------------------------------------------ elementwise + column sum
@@ -1465,7 +1516,8 @@ def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfu
     """A fused node to its kernel, every other node to its plain launch (src/fusion/lower-fused.js:32-45).
 
     `fold` (resident programs only): transposeLast2 nodes read only as tensor-core GEMM operands get no
-    launch; the GEMM's operand split reads their source.  Their values then never exist on the device,
+    launch; the GEMM's operand split reads their source; a GEMM read only by a transposeLast2 computes
+    the transposed product itself (transposed_products).  Their values then never exist on the device,
     so verification runs that read back every node lower without it.
     `colfuse` (resident programs only): a sum over axis 0 runs in its elementwise producer's launch
     (colsum_fusions), and so does a sum over the last axis of enough rows (rowsum_fusions); a producer
@@ -1475,16 +1527,21 @@ def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfu
     computed in its elementwise producer's launch, both stored (mo_fusions).
     """
     folds = foldable_transposes(graph, matmul, keep) if fold else set()
+    tprods = transposed_products(graph, matmul, keep, folds) if fold else {}
+    tmats = set(tprods.values())
     cols = colsum_fusions(graph, keep) if colfuse else {}
     rows = rowsum_fusions(graph, keep, exclude=set(cols) | {p for p, _ in cols.values()}) if colfuse else {}
     sums = {**{sid: (p, w, _colsum_launch) for sid, (p, w) in cols.items()},
             **{sid: (p, w, _rowsum_launch) for sid, (p, w) in rows.items()}}
     producer_of = {p: (sid, w, f) for sid, (p, w, f) in sums.items()}
-    mos = mo_fusions(graph, keep, exclude=set(sums) | set(producer_of) | folds) if mofuse else {}
+    mos = mo_fusions(graph, keep, exclude=set(sums) | set(producer_of) | folds | set(tprods) | tmats) if mofuse else {}
     readers = set(mos.values())
     launches = []
     for node in graph.nodes:
-        if node.op in ("input", "const") or node.id in folds or node.id in readers:
+        if node.op in ("input", "const") or node.id in folds or node.id in readers or node.id in tmats:
+            continue
+        if node.id in tprods:             # a GEMM read only by a transpose: the transposed product
+            launches.append(_transposed_product_launch(graph, node, graph.nodes[tprods[node.id]], matmul, folds))
             continue
         if node.id in mos:                # a producer computing its reader too
             launches.append(_mo_launch(graph, node, graph.nodes[mos[node.id]]))
@@ -1508,4 +1565,4 @@ def lower_fused(graph, matmul="naive", sabotage=None, fold=False, keep=(), colfu
             lau = _plain_launch(graph, node, matmul)
         lau.bytes = _bytes(graph, lau)
         launches.append(lau)
-    return {"launches": launches, "folded": sorted(folds)}
+    return {"launches": launches, "folded": sorted(folds), "transposed": sorted(tprods.items())}

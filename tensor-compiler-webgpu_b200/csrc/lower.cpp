@@ -947,7 +947,7 @@ struct Mnk {
 };
 
 static std::string epilogue_source(const Graph& body, int out_id, const std::string& sabotage, bool tc, i64 bn, bool a_t,
-                                   bool b_t, Mnk* mnk) {
+                                   bool b_t, Mnk* mnk, bool cross_ba = false) {
   const Node* root = nullptr;
   for (auto& n : body.nodes)
     if (n.op == "matmul") {
@@ -1015,7 +1015,8 @@ static std::string epilogue_source(const Graph& body, int out_id, const std::str
               "\n#define TCB_PART_OFFSET " + std::to_string(part_off) + "ull\n" + "#define TCB_GRID " +
               std::to_string(tp.grid) + "\n#define TCB_TAIL_SPLIT " + std::to_string(tp.tail) + "\n" +
               "#define TCB_TAIL_OFFSET " + std::to_string(tp.tail_off) + "ull\n" + "#define TCB_A_T " +
-              std::to_string((int)a_t) + "\n#define TCB_B_T " + std::to_string((int)b_t) + "\n";
+              std::to_string((int)a_t) + "\n#define TCB_B_T " + std::to_string((int)b_t) + "\n" +
+              (cross_ba ? "#define TCB_CROSS_BA 1\n" : "");
   }
   *mnk = {batch, M, K, N};
   std::string kernel = tc ? "tcgen05" : "simt";
@@ -1050,12 +1051,12 @@ static bool uses_tensor_cores(const std::vector<i64>& a_shape, const std::string
 
 static Launch tc_epilogue_launch(const Graph& body, int out_id, int node_id, const std::string& op, const std::string& kind,
                                  const std::string* pattern, const std::vector<int>& inputs, const std::string& sabotage,
-                                 bool a_t, bool b_t) {
+                                 bool a_t, bool b_t, bool cross_ba = false) {
   const Node& root = matmul_root(body);
   i64 bn = gemm_bn(body.nodes[root.inputs[1]].shape.back());
   Mnk m;
   Launch l;
-  l.code = epilogue_source(body, out_id, sabotage, true, bn, a_t, b_t, &m);
+  l.code = epilogue_source(body, out_id, sabotage, true, bn, a_t, b_t, &m, cross_ba);
   i64 batch = m.batch, M = m.M, K = m.K, N = m.N;
   if (batch > 65535 || cdiv(M, GEMM_BM) > 65535) throw Error("matmul grid too large");
   i64 Kp = kpad(K);
@@ -1124,10 +1125,10 @@ static Launch tc_epilogue_launch(const Graph& body, int out_id, int node_id, con
 
 static Launch epilogue_launch(const Graph& body, int out_id, int node_id, const std::string& op, const std::string& kind,
                               const std::string* pattern, const std::vector<int>& inputs, const std::string& matmul,
-                              const std::string& sabotage, bool a_t, bool b_t) {
+                              const std::string& sabotage, bool a_t, bool b_t, bool cross_ba = false) {
   const Node& root = matmul_root(body);
   if (uses_tensor_cores(body.nodes[root.inputs[0]].shape, matmul))
-    return tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage, a_t, b_t);
+    return tc_epilogue_launch(body, out_id, node_id, op, kind, pattern, inputs, sabotage, a_t, b_t, cross_ba);
   if (a_t || b_t) throw Error("transposed operands are folded only on the tensor-core path");
   Mnk m;
   Launch l;
@@ -1291,6 +1292,47 @@ static Launch folded_launch(Lowering& L, const Node& node, const std::string& ma
   l.inputs.clear();
   bool t;
   for (int i : node.inputs) l.inputs.push_back(unfold(i, &t));
+  return l;
+}
+
+// A plain tensor-core matmul read only by a transposeLast2 (that does not itself fold into a GEMM):
+// the pair becomes one GEMM computing the transposed product, (A.B)^T = B^T.A^T.
+static std::map<int, int> transposed_products(const Graph& g, const std::string& matmul, const std::set<int>& keep,
+                                              const std::set<int>& folds) {
+  std::map<int, std::vector<int>> consumers;
+  for (auto& n : g.nodes)
+    for (int i : n.inputs) consumers[i].push_back(n.id);
+  std::map<int, int> out;
+  for (auto& T : g.nodes) {
+    if (T.op != "transpose" || !is_last2_swap(T) || folds.count(T.id)) continue;
+    const Node& M = g.nodes[T.inputs[0]];
+    if (M.op != "matmul" || keep.count(M.id) || consumers[M.id] != std::vector<int>{T.id} ||
+        !uses_tensor_cores(g.nodes[M.inputs[0]].shape, matmul))
+      continue;
+    out[T.id] = M.id;
+  }
+  return out;
+}
+
+static Launch transposed_product_launch(Lowering& L, const Node& T, const Node& M, const std::string& matmul,
+                                        const std::set<int>& folds) {
+  const Graph& g = *L.graph;
+  auto unfold = [&](int i, bool* t) {
+    *t = false;
+    while (folds.count(i)) { i = g.nodes[i].inputs[0]; *t = !*t; }
+    return i;
+  };
+  bool a_t = false, b_t = false;
+  int a_src = unfold(M.inputs[0], &a_t), b_src = unfold(M.inputs[1], &b_t);
+  std::vector<i64> sa = g.nodes[M.inputs[0]].shape, sb = g.nodes[M.inputs[1]].shape;
+  std::swap(sa[sa.size() - 1], sa[sa.size() - 2]);
+  std::swap(sb[sb.size() - 1], sb[sb.size() - 2]);
+  int out;
+  auto body = one_op_body(M, {sb, sa}, &out);
+  Launch l = epilogue_launch(*body, out, T.id, "matmul", "matmul-" + matmul, nullptr, {b_src, a_src}, matmul, "", !b_t,
+                             !a_t, true);
+  l.inputs = {b_src, a_src};
+  l.bytes = launch_bytes(g, l);
   return l;
 }
 
@@ -1632,6 +1674,9 @@ struct Options {
 static void lower_graph(Lowering& L, const Options& o) {
   const Graph& g = *L.graph;
   std::set<int> folds = o.fold ? foldable_transposes(g, o.matmul, o.keep) : std::set<int>();
+  std::map<int, int> tprods = o.fold ? transposed_products(g, o.matmul, o.keep, folds) : std::map<int, int>();
+  std::set<int> tmats;
+  for (auto& kv : tprods) tmats.insert(kv.second);
   std::map<int, std::pair<int, bool>> cols = (o.fused && o.colfuse) ? colsum_fusions(g, o.keep)
                                                                      : std::map<int, std::pair<int, bool>>();
   std::map<int, std::pair<int, bool>> rows;
@@ -1651,12 +1696,19 @@ static void lower_graph(Lowering& L, const Options& o) {
     std::set<int> exclude(folds.begin(), folds.end());
     for (auto& kv : sums) exclude.insert(kv.first);
     for (auto& kv : producer_of) exclude.insert(kv.first);
+    for (auto& kv : tprods) { exclude.insert(kv.first); exclude.insert(kv.second); }
     mos = mo_fusions(g, o.keep, exclude);
   }
   std::set<int> readers;
   for (auto& kv : mos) readers.insert(kv.second);
   for (auto& node : g.nodes) {
-    if (node.op == "input" || node.op == "const" || folds.count(node.id) || readers.count(node.id)) continue;
+    if (node.op == "input" || node.op == "const" || folds.count(node.id) || readers.count(node.id) ||
+        tmats.count(node.id))
+      continue;
+    if (tprods.count(node.id)) {  // a GEMM read only by a transpose: the transposed product
+      L.launches.push_back(transposed_product_launch(L, node, g.nodes[tprods[node.id]], o.matmul, folds));
+      continue;
+    }
     if (mos.count(node.id)) {
       L.launches.push_back(mo_launch(g, node, g.nodes[mos[node.id]]));
       continue;
@@ -1682,6 +1734,7 @@ static void lower_graph(Lowering& L, const Options& o) {
     L.launches.push_back(std::move(l));
   }
   L.folded.assign(folds.begin(), folds.end());
+  L.transposed.assign(tprods.begin(), tprods.end());
 }
 
 // ---------------------------------------------------------------- records as JSON
@@ -1800,7 +1853,10 @@ int tc_lowered_json(tc_lowered* l, char* json, uint64_t cap, uint64_t* needed) {
   if (l->json.empty()) {
     std::string s = "{\"launches\":[";
     for (size_t k = 0; k < l->L.launches.size(); ++k) s += (k ? "," : "") + tcl::launch_json(l->L.launches[k]);
-    s += "],\"folded\":" + tcl::ints_json(l->L.folded) + "}";
+    s += "],\"folded\":" + tcl::ints_json(l->L.folded) + ",\"transposed\":[";
+    for (size_t k = 0; k < l->L.transposed.size(); ++k)
+      s += (k ? ",[" : "[") + std::to_string(l->L.transposed[k].first) + "," + std::to_string(l->L.transposed[k].second) + "]";
+    s += "]}";
     l->json = std::move(s);
   }
   if (needed) *needed = l->json.size() + 1;

@@ -79,6 +79,7 @@ struct Lowering {
   std::shared_ptr<Graph> graph;
   std::vector<Launch> launches;
   std::vector<int> folded;
+  std::vector<std::pair<int, int>> transposed;  // (transposeLast2, matmul) computed as one transposed product
   std::map<std::string, Launch> plain_cache;
 };
 

@@ -47,6 +47,9 @@ struct GemmParams {
 #ifndef TCB_BK
 #define TCB_BK 32
 #endif
+#ifndef TCB_CROSS_BA
+#define TCB_CROSS_BA 0  // 1: issue A_hi.B_lo before A_lo.B_hi (a GEMM computing (X.Y)^T as Y^T.X^T)
+#endif
 // K-block: 32 fp32 (128-byte rows, 128-byte swizzle) or 16 fp32 (64-byte rows, 64-byte swizzle).
 constexpr int GB_M = 128, GB_K = TCB_BK;
 static_assert(GB_K == 32 || GB_K == 16, "K-block of 16 or 32 floats");
@@ -464,8 +467,13 @@ extern "C" __global__ void __launch_bounds__((TCB_FS_A || TCB_FS_B) ? 320 : 192,
           for (int k = 0; k < GB_K / 8; ++k) {
             const u64 ah = da(st, k), al = da(st + A_BYTES, k);
             const u64 bh = db(st + 2 * A_BYTES, k), bl = db(st + 2 * A_BYTES + B_BYTES, k);
-            mma_tf32(acc, al, bh, ID, (kb | k) != 0);
-            mma_tf32(acc, ah, bl, ID, 1);
+            if (TCB_CROSS_BA) {  // a transposed product: the mixed terms in the order of the untransposed one
+              mma_tf32(acc, ah, bl, ID, (kb | k) != 0);
+              mma_tf32(acc, al, bh, ID, 1);
+            } else {
+              mma_tf32(acc, al, bh, ID, (kb | k) != 0);
+              mma_tf32(acc, ah, bl, ID, 1);
+            }
             mma_tf32(acc, ah, bh, ID, 1);
           }
           mma_commit(empty(s));

@@ -251,3 +251,52 @@ def test_plain_launch_cache_follows_the_gemm_overrides(pkg, monkeypatch):
     monkeypatch.setenv("TCB_GEMM_FUSED", "0")
     (b,) = cg.lower(g, matmul="tiled")["launches"]
     assert a.info["fused_split"] == (True, True) and b.info["fused_split"] == (False, False)
+
+
+def test_transposed_products(cg):
+    """A plain tensor-core matmul read only by a transposeLast2 becomes one GEMM computing the transposed
+    product (B^T.A^T, operands through their folds, the mixed 3xTF32 terms in the untransposed order);
+    not when the matmul is kept or read elsewhere, when the transpose itself folds into a GEMM, or on the
+    CUDA-core path."""
+    import importlib
+    ir = importlib.import_module("tensor-compiler-webgpu_b200.ir")
+    g = ir.Graph()
+    a = g.input("a", [4, 64, 256])
+    b = g.input("b", [4, 256, 256])
+    m = g.matmul(a, b)                          # [4, 64, 256], read only by t
+    t = g.transpose(m, [0, 2, 1])               # [4, 256, 64]
+    out = g.relu(t)
+    m2 = g.matmul(a, b)
+    t2 = g.transpose(m2, [0, 2, 1])
+    shared = g.exp(m2)                          # m2 has another reader: no rewrite
+    m3 = g.matmul(a, b)
+    t3 = g.transpose(m3, [0, 2, 1])
+    w = g.input("w", [4, 64, 32])
+    prod = g.matmul(t3, w)                      # t3 folds into this GEMM's operand instead
+    keep = [out, t2, shared, prod]
+    low = cg.lower_fused(g, matmul="tiled", fold=True, keep=keep)
+    assert low["transposed"] == [(t, m)]
+    lau = next(l for l in low["launches"] if l.node == t)
+    assert lau.inputs == [b, a] and lau.info["mnk"] == (4, 256, 256, 64)
+    assert (lau.info["a_t"], lau.info["b_t"]) == (True, True)
+    assert "#define TCB_CROSS_BA 1" in lau.code
+    assert m not in {l.node for l in low["launches"]}
+    assert cg.lower_fused(g, matmul="tiled", fold=True, keep=keep + [m])["transposed"] == []
+    assert cg.lower_fused(g, matmul="naive", fold=True, keep=keep)["transposed"] == []
+    assert cg.lower_fused(g, matmul="tiled", keep=keep)["transposed"] == []
+
+
+def test_c5_attention_products_transposed(pkg, cg):
+    import importlib
+    wl = importlib.import_module("tensor-compiler-webgpu_b200.workloads")
+    cfg, c = wl.c5_cfg(batch=64)
+    gs = pkg.steps.build_grad3b(c["V"], 64, cfg)
+    k0 = [gs["loss"], *gs["grads"].values()]
+    f = pkg.fuse.fuse(gs["graph"], keep=k0)
+    keep = [f.index[i] for i in k0]
+    low = cg.lower_fused(f.graph, matmul="tiled", fold=True, keep=keep, colfuse=True, mofuse=True)
+    tl = {t: m for t, m in low["transposed"]}
+    assert len(tl) == cfg["L"]
+    for l in low["launches"]:
+        if l.node in tl:
+            assert l.info["mnk"][1:] == (256, 256, 64) and l.info["bn"] == 64

@@ -100,7 +100,8 @@ def _small_transformer(wl):
 
 
 def _keep_all(rt, runner, graph, lowered):
-    ids = [n.id for n in graph.nodes if n.op not in ("input", "const") and n.id not in set(lowered["folded"])]
+    gone = set(lowered["folded"]) | {m for _, m in lowered.get("transposed", [])}
+    ids = [n.id for n in graph.nodes if n.op not in ("input", "const") and n.id not in gone]
     return rt.Program(runner, graph, lowered, keep=ids, batch=True), ids
 
 
@@ -109,6 +110,9 @@ def _node_local(pkg, oracle, graph, lowered, feed, got):
     GPU value of every launched node, `feed` the inputs' float32 values."""
     vals = [None] * len(graph.nodes)
     folded = set(lowered["folded"])
+    # a matmul computed as its reader's transposed product has no launch of its own: its value is that
+    # transpose's GPU value transposed back (no arithmetic), and the matmul is judged on it
+    tmat = {m: t for t, m in lowered.get("transposed", [])}
     for n in graph.nodes:
         if n.op == "input":
             vals[n.id] = np.asarray(feed[n.attrs["name"]], np.float32).reshape(-1).astype(np.float64)
@@ -119,6 +123,9 @@ def _node_local(pkg, oracle, graph, lowered, feed, got):
         elif n.id in folded:   # no launch: the transpose of its source, moved on the host (no arithmetic)
             src = graph.nodes[n.inputs[0]]
             vals[n.id] = vals[src.id].reshape(src.shape).transpose(n.attrs["perm"]).reshape(-1)
+        elif n.id in tmat:
+            t = graph.nodes[tmat[n.id]]
+            vals[n.id] = got[t.id].astype(np.float64).reshape(t.shape).transpose(t.attrs["perm"]).reshape(-1)
         else:
             vals[n.id] = got[n.id].astype(np.float64)
     expected, bound = oracle.local_reference_fused(graph, vals)

@@ -58,6 +58,7 @@ def _compare(lib, cg, graph, fused=True, **opts):
         py = cg.lower(graph, **{k: v for k, v in opts.items() if k in ("matmul", "sabotage", "fold", "keep")})
     c = c_lower(lib, graph, fused=fused, **{k: (list(v) if k == "keep" else v) for k, v in opts.items()})
     assert c["folded"] == list(py["folded"])
+    assert c.get("transposed", []) == [list(p) for p in py.get("transposed", [])]
     assert len(c["launches"]) == len(py["launches"])
     for k, (a, b) in enumerate(zip(py["launches"], c["launches"])):
         want = _py_record(a)
