@@ -656,7 +656,9 @@ def main():
     ap.add_argument("--workload", default="all", choices=["all", "c1", "c2", "c4", "c3", "c5"])
     ap.add_argument("--batch", type=int, default=None, help="C5 global batch (default 512)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=10,
+                    help="steps of the end-to-end measurement (copies overlap across steps: the first step's "
+                         "input copy and the last one's output copy are the pipeline's fill and drain)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--rows", type=int, default=None, help="cut C2/C4 to fewer rows (profiling cases only)")
