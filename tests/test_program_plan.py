@@ -294,3 +294,29 @@ def test_bucketed_allreduce_plan(pkg, recorded, world, buckets, full):
     # the layout follows the order in which the backward finishes the gradients
     at = [gp.ptrs[tr.fg.index[tr.gs["grads"][n]]] for n in tr.order]
     assert at == sorted(at)
+
+
+@pytest.mark.parametrize("sizes,buckets", [([100, 300, 1000, 4, 5000, 256], 4), ([100], 4), ([100, 200], 1),
+                                           ([4096] * 58, 4), ([262144 * 4, 1024, 1024, 262144 * 4], 3)])
+def test_bucket_layout(sizes, buckets):
+    """The flat gradient buffer's layout: 256-byte aligned slices back to back, at most `buckets`
+    contiguous spans that cover it exactly, each cut at a tensor boundary."""
+    dp = importlib.import_module("tensor-compiler-webgpu_b200.dp")
+    offs, spans = dp.bucket_layout(sizes, buckets)
+    assert offs[0] == 0 and all(o % 256 == 0 for o in offs)
+    assert all(b - a >= n for a, b, n in zip(offs, offs[1:], sizes))
+    total = offs[-1] + (sizes[-1] + 255) // 256 * 256
+    assert 1 <= len(spans) <= buckets
+    assert spans[0][0] == 0 and spans[-1][1] == total and spans[0][2] == 0 and spans[-1][3] == len(sizes)
+    for (lo, hi, a, b), nxt in zip(spans, spans[1:] + [None]):
+        assert lo == offs[a] and a < b and (hi == offs[b] if b < len(sizes) else hi == total)
+        if nxt is not None:
+            assert nxt[0] == hi and nxt[2] == b
+
+
+def test_one_wave_share():
+    rt = importlib.import_module("tensor-compiler-webgpu_b200.runtime")
+    cg = importlib.import_module("tensor-compiler-webgpu_b200.codegen")
+    for members in (1, 2, 8, 51, 176, 2000):
+        gx = rt.one_wave_share(members)
+        assert gx >= 1 and (gx - 1) * members < cg.SM_COUNT * 8 <= gx * members or gx == 1
